@@ -1,0 +1,273 @@
+"""GPU parity of the four kernels against the CPU oracle (called through the C ABI).
+
+Tolerances: bf16/f16 attention within max-abs 2e-2 and
+mean-abs 2e-3 of the fp32 oracle; fp32 attention within 1e-4; KV writes and metadata
+bit-exact.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import paged as ref
+
+pytestmark = pytest.mark.gpu
+
+BF16_MAX, BF16_MEAN = 2e-2, 2e-3
+F32_MAX = 1e-4
+
+
+def make_pool(seed, layers, num_blocks, bs, hkv, d, dtype):
+    g = torch.Generator().manual_seed(seed)
+    kc = torch.randn(layers, num_blocks * bs, hkv, d, generator=g).to(dtype)
+    vc = torch.randn(layers, num_blocks * bs, hkv, d, generator=g).to(dtype)
+    return kc, vc
+
+
+def make_tables(seed, ctx, bs, num_blocks):
+    rng = np.random.default_rng(seed)
+    perm = rng.permutation(num_blocks)
+    tables, used = [], 0
+    for c in ctx:
+        n = (c + bs - 1) // bs
+        tables.append(perm[used:used + n].tolist())
+        used += n
+    assert used <= num_blocks
+    width = max(1, max(len(t) for t in tables))
+    bt = np.full((len(ctx), width), -1, dtype=np.int32)
+    for i, t in enumerate(tables):
+        bt[i, :len(t)] = t
+    return tables, torch.from_numpy(bt)
+
+
+def close(got, expect, dtype):
+    err = (got.float().cpu() - expect).abs()
+    if dtype == torch.float32:
+        assert err.max().item() < F32_MAX, err.max().item()
+    else:
+        assert err.max().item() < BF16_MAX, err.max().item()
+        assert err.mean().item() < BF16_MEAN, err.mean().item()
+
+
+# ------------------------------------------------------------------ K1 KV write
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_kv_write_bit_exact_with_hf_layout(ops, dtype):
+    dev = torch.device("cuda")
+    layers, nb, bs, hkv, d = 3, 40, 16, 2, 64
+    kc, vc = make_pool(1, layers, nb, bs, hkv, d, dtype)
+    n = 57
+    g = torch.Generator().manual_seed(2)
+    # HF states are (1, kv_heads, tokens, head_dim); the cache adapter hands the kernel
+    # the transposed (tokens, kv_heads, head_dim) view, as hf_batched_paged_cache.py:115.
+    hf_k = torch.randn(1, hkv, n, d, generator=g).to(dtype)
+    hf_v = torch.randn(1, hkv, n, d, generator=g).to(dtype)
+    slots = torch.randperm(nb * bs, generator=g)[:n].to(torch.int32)
+    kd, vd = kc.to(dev), vc.to(dev)
+    ops.kv_write(kd, vd, 2, slots.to(dev), hf_k.to(dev)[0].transpose(0, 1),
+                 hf_v.to(dev)[0].transpose(0, 1))
+    ref.scatter(kc, vc, 2, slots.tolist(), hf_k[0].transpose(0, 1), hf_v[0].transpose(0, 1))
+    assert torch.equal(kd.cpu(), kc) and torch.equal(vd.cpu(), vc)
+
+
+def test_kv_write_skips_padding_and_flags_out_of_range(ops):
+    dev = torch.device("cuda")
+    kc, vc = make_pool(3, 1, 8, 16, 2, 128, torch.bfloat16)
+    keys = torch.randn(4, 2, 128).to(torch.bfloat16)
+    vals = torch.randn(4, 2, 128).to(torch.bfloat16)
+    slots = torch.tensor([5, -1, 9, 8 * 16 + 3], dtype=torch.int32)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    kd, vd = kc.to(dev), vc.to(dev)
+    ops.kv_write(kd, vd, 0, slots.to(dev), keys.to(dev), vals.to(dev), err)
+    ref.scatter(kc, vc, 0, [5, 9], keys[[0, 2]], vals[[0, 2]])
+    assert torch.equal(kd.cpu(), kc) and torch.equal(vd.cpu(), vc)
+    assert int(err.item()) & 1  # B2P_DEV_SLOT_RANGE
+
+
+def test_kv_write_rejects_bad_layer(ops):
+    dev = torch.device("cuda")
+    kc, vc = make_pool(3, 2, 4, 16, 2, 64, torch.float16)
+    k = torch.zeros(1, 2, 64, dtype=torch.float16, device=dev)
+    with pytest.raises(ValueError):
+        ops.kv_write(kc.to(dev), vc.to(dev), 2, torch.zeros(1, dtype=torch.int32, device=dev),
+                     k, k)
+
+
+# ------------------------------------------------------------------ K2 decode
+DECODE_SHAPES = [
+    # (hq, hkv, d, bs)
+    (12, 2, 128, 16),   # Qwen2.5-1.5B
+    (14, 2, 64, 16),    # Qwen2.5-0.5B
+    (28, 4, 128, 16),   # Qwen2.5-7B
+    (12, 2, 128, 32),   # two sub-blocks per block
+    (8, 1, 128, 16),    # group of 8
+    (32, 2, 128, 16),   # group of 16 (two query-head tiles)
+    (4, 4, 64, 16),     # no GQA
+]
+
+
+@pytest.mark.parametrize("shape", DECODE_SHAPES)
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_decode_matches_oracle(ops, shape, dtype):
+    hq, hkv, d, bs = shape
+    dev = torch.device("cuda")
+    ctx = [1, 15, 16, 17, 33, 100, 511, 1024, 2049, 3000]
+    nb = sum((c + bs - 1) // bs for c in ctx) + 7
+    kc, vc = make_pool(10, 2, nb, bs, hkv, d, dtype)
+    tables, bt = make_tables(11, ctx, bs, nb)
+    q = torch.randn(len(ctx), hq, d, generator=torch.Generator().manual_seed(12)).to(dtype)
+    out = ops.paged_decode(q.to(dev), kc.to(dev), vc.to(dev), 1, bt.to(dev),
+                           torch.tensor(ctx, dtype=torch.int32, device=dev), bs, d ** -0.5)
+    expect = ref.decode_attention(q, kc, vc, 1, tables, ctx, bs, d ** -0.5)
+    close(out, expect, dtype)
+
+
+@pytest.mark.parametrize("bs,d", [(16, 128), (8, 64), (1, 32), (16, 96)])
+def test_decode_fp32_and_generic_shapes(ops, bs, d):
+    dev = torch.device("cuda")
+    hq, hkv = 14, 2
+    ctx = [1, 7, 64, 130]
+    nb = sum((c + bs - 1) // bs for c in ctx) + 3
+    for dtype in (torch.float32, torch.bfloat16):
+        kc, vc = make_pool(20, 1, nb, bs, hkv, d, dtype)
+        tables, bt = make_tables(21, ctx, bs, nb)
+        q = torch.randn(len(ctx), hq, d, generator=torch.Generator().manual_seed(22)).to(dtype)
+        out = ops.paged_decode(q.to(dev), kc.to(dev), vc.to(dev), 0, bt.to(dev),
+                               torch.tensor(ctx, dtype=torch.int32, device=dev), bs, d ** -0.5)
+        close(out, ref.decode_attention(q, kc, vc, 0, tables, ctx, bs, d ** -0.5), dtype)
+
+
+def test_decode_many_short_sequences_cross_cta_merge(ops):
+    """Hundreds of sequences of mixed lengths: ranges cut sequences in many places."""
+    dev = torch.device("cuda")
+    hq, hkv, d, bs = 12, 2, 128, 16
+    rng = np.random.default_rng(5)
+    ctx = rng.integers(1, 6000, size=300).tolist()
+    nb = sum((c + bs - 1) // bs for c in ctx) + 1
+    kc, vc = make_pool(30, 1, nb, bs, hkv, d, torch.bfloat16)
+    tables, bt = make_tables(31, ctx, bs, nb)
+    q = torch.randn(len(ctx), hq, d, generator=torch.Generator().manual_seed(32)).to(torch.bfloat16)
+    ws = ops.make_decode_workspace(len(ctx), hq, hkv, d, dev)
+    args = (q.to(dev), kc.to(dev), vc.to(dev), 0, bt.to(dev),
+            torch.tensor(ctx, dtype=torch.int32, device=dev), bs, d ** -0.5)
+    out1 = ops.paged_decode(*args, workspace=ws).clone()
+    out2 = ops.paged_decode(*args, workspace=ws)
+    assert torch.equal(out1, out2)  # deterministic, and the workspace resets itself
+    n_counters = hkv * len(ctx)
+    assert int(ws.view(torch.int32)[:n_counters].abs().sum().item()) == 0
+    close(out1, ref.decode_attention(q, kc, vc, 0, tables, ctx, bs, d ** -0.5), torch.bfloat16)
+
+
+def test_decode_garbage_past_context_is_masked(ops):
+    """Slots past a sequence's length may hold NaN/Inf (the pool is not cleared)."""
+    dev = torch.device("cuda")
+    hq, hkv, d, bs = 12, 2, 128, 16
+    ctx = [5, 21]
+    kc, vc = make_pool(40, 1, 4, bs, hkv, d, torch.bfloat16)
+    tables = [[2], [0, 3]]
+    bt = torch.tensor([[2, -1], [0, 3]], dtype=torch.int32)
+    kc[0, 2 * bs + 5:3 * bs] = float("nan")
+    vc[0, 2 * bs + 5:3 * bs] = float("inf")
+    vc[0, 3 * bs + 5:4 * bs] = float("nan")
+    q = torch.randn(2, hq, d, generator=torch.Generator().manual_seed(41)).to(torch.bfloat16)
+    out = ops.paged_decode(q.to(dev), kc.to(dev), vc.to(dev), 0, bt.to(dev),
+                           torch.tensor(ctx, dtype=torch.int32, device=dev), bs, d ** -0.5)
+    assert torch.isfinite(out.float()).all()
+    close(out, ref.decode_attention(q, kc, vc, 0, tables, ctx, bs, d ** -0.5), torch.bfloat16)
+
+
+def test_decode_out_of_range_block_is_flagged(ops):
+    dev = torch.device("cuda")
+    hq, hkv, d, bs = 12, 2, 128, 16
+    kc, vc = make_pool(50, 1, 4, bs, hkv, d, torch.bfloat16)
+    bt = torch.tensor([[1, 99]], dtype=torch.int32)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    q = torch.randn(1, hq, d).to(torch.bfloat16)
+    ops.paged_decode(q.to(dev), kc.to(dev), vc.to(dev), 0, bt.to(dev),
+                     torch.tensor([20], dtype=torch.int32, device=dev), bs, d ** -0.5,
+                     err_flag=err)
+    assert int(err.item()) & 2  # B2P_DEV_BLOCK_RANGE
+
+
+def test_decode_full_benchmark_workload(ops):
+    """The benchmark's 256-sequence, 65,536-block workload at full size."""
+    import bench
+
+    dev = torch.device("cuda")
+    w = bench.make_workload(1234, None)
+    kd, vd = w["kc"].to(dev), w["vc"].to(dev)
+    ops.kv_write(kd, vd, 0, torch.from_numpy(w["slots"]).to(dev), w["new_k"].to(dev),
+                 w["new_v"].to(dev))
+    out = ops.paged_decode(w["q"].to(dev), kd, vd, 0, torch.from_numpy(w["tables"]).to(dev),
+                           torch.from_numpy(w["ctx"]).to(dev), bench.BLOCK_SIZE,
+                           bench.HEAD_DIM ** -0.5)
+    kc, vc = w["kc"], w["vc"]
+    ref.scatter(kc, vc, 0, w["slots"].tolist(), w["new_k"], w["new_v"])
+    tables = [row[row >= 0].tolist() for row in w["tables"]]
+    expect = ref.decode_attention(w["q"], kc, vc, 0, tables, w["ctx"].tolist(), bench.BLOCK_SIZE,
+                                  bench.HEAD_DIM ** -0.5)
+    close(out, expect, torch.bfloat16)
+
+
+# ------------------------------------------------------------------ K3 prefill
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("shape", [(12, 2, 128, 16), (14, 2, 64, 16), (28, 4, 128, 32)])
+def test_prefill_matches_oracle(ops, dtype, shape):
+    hq, hkv, d, bs = shape
+    dev = torch.device("cuda")
+    # whole-history prefills plus two chunked-prefill runs (q_len < ctx)
+    ctx = [1, 17, 64, 130, 300, 77]
+    qlen = [1, 17, 64, 130, 45, 1]
+    cu = np.concatenate([[0], np.cumsum(qlen)]).tolist()
+    nb = sum((c + bs - 1) // bs for c in ctx) + 2
+    kc, vc = make_pool(60, 1, nb, bs, hkv, d, dtype)
+    tables, bt = make_tables(61, ctx, bs, nb)
+    q = torch.randn(cu[-1], hq, d, generator=torch.Generator().manual_seed(62)).to(dtype)
+    out = ops.paged_prefill(q.to(dev), kc.to(dev), vc.to(dev), 0, bt.to(dev),
+                            torch.tensor(cu, dtype=torch.int32, device=dev),
+                            torch.tensor(ctx, dtype=torch.int32, device=dev), max(qlen), bs,
+                            d ** -0.5)
+    close(out, ref.prefill_attention(q, kc, vc, 0, tables, cu, ctx, bs, d ** -0.5), dtype)
+
+
+# ------------------------------------------------------------------ K4 metadata
+def test_metadata_bit_exact(ops):
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(70)
+    bs = 16
+    n = 37
+    lengths = rng.integers(1, 300, size=n)
+    phases = [ref.PREFILL if rng.random() < 0.3 else ref.DECODE for _ in range(n)]
+    # decode executions come first, as in Engine.step (engine.py:156-171)
+    order = sorted(range(n), key=lambda i: phases[i] != ref.DECODE)
+    phases = [phases[i] for i in order]
+    lengths = [int(lengths[i]) for i in order]
+    mirror_rows = n + 5
+    width = 32
+    perm = rng.permutation(4096)
+    mirror = np.full((mirror_rows, width), -1, dtype=np.int32)
+    rows = rng.permutation(mirror_rows)[:n]
+    used = 0
+    tables = []
+    for i, L in enumerate(lengths):
+        nb = (L + bs - 1) // bs
+        mirror[rows[i], :nb] = perm[used:used + nb]
+        tables.append(perm[used:used + nb].tolist())
+        used += nb
+    qlens = [ref.query_length(p, L) for p, L in zip(phases, lengths)]
+    total_q = sum(qlens)
+    md = ops.build_metadata(torch.tensor(qlens, dtype=torch.int32, device=dev),
+                            torch.tensor(lengths, dtype=torch.int32, device=dev),
+                            torch.tensor(rows, dtype=torch.int32, device=dev),
+                            torch.from_numpy(mirror).to(dev), bs, total_q, width)
+    lay = ref.batch_layout(phases, lengths)
+    assert md["cu_seqlens_q"].cpu().tolist() == [*lay["query_offsets"], lay["total_query_tokens"]]
+    assert md["cu_seqlens_k"].cpu().tolist() == [*lay["key_offsets"], lay["total_key_tokens"]]
+    assert md["logit_indices"].cpu().tolist() == list(lay["logit_indices"])
+    assert md["positions"].cpu().numpy().tolist() == ref.packed_positions(phases, lengths).tolist()
+    hist = [ref.history_slots(t, L, bs) for t, L in zip(tables, lengths)]
+    assert md["slot_mapping"].cpu().numpy().tolist() == ref.write_slots(phases, hist).tolist()
+    bt = md["block_tables"].cpu().numpy()
+    for i, t in enumerate(tables):
+        assert bt[i, :len(t)].tolist() == t and (bt[i, len(t):] == -1).all()
