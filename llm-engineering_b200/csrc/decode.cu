@@ -12,30 +12,28 @@
 // Design (HBM-bound: 1 KiB of K+V per token for 2 KV heads x 128 dims in bf16):
 //  * Work space = for each KV head, the flattened list of 16-slot sub-blocks of all
 //    sequences (a 16-slot sub-block is contiguous in the pool because a block's slots are
-//    consecutive). Each KV head's list is cut into gridDim.x equal ranges, one per CTA
-//    (stream-K), so every CTA streams the same number of bytes whatever the context-length
-//    mix; a sequence cut by a range boundary is finished by the last CTA that works on it
-//    (counter in the workspace), which merges the partial softmax states.
-//  * One producer thread walks the CTA's range, reads block-table entries and issues TMA
-//    tile loads (K and V sub-block of one head: 2 x 16 x head_dim elements) into a ring of
-//    NS shared-memory stages guarded by mbarriers (full: TMA bytes landed; empty: the
-//    consumer warp is done).
-//  * Four consumer warps take sub-blocks round-robin. Per sub-block a warp computes
-//    S^T = K Q^T on the tensor cores (m16n8k16: 16 tokens x 8 query heads of the GQA group,
-//    K loaded with ldmatrix from the 128-byte-swizzled tile), the online softmax in fp32
-//    (warp shuffles over the 8 lanes that share a query head), and O^T += V^T P^T (V^T from
+//    consecutive). Each KV head's list is cut into equal ranges, one per WARP (stream-K at
+//    warp granularity), so every warp streams the same number of bytes whatever the
+//    context-length mix. Warps of a CTA never wait for one another.
+//  * Each warp owns a private ring of S shared-memory stages. Lane 0 issues TMA tile loads
+//    (K and V sub-block of one head: 2 x 16 x head_dim elements, 128-byte swizzle, no
+//    multicast) and refills a stage as soon as the warp has consumed it; the physical
+//    block of every upcoming sub-block is resolved 32 at a time with parallel loads, one
+//    chunk ahead, so no TMA waits on a dependent global load.
+//  * Per sub-block the warp computes S^T = K Q^T on the tensor cores (m16n8k16: 16 tokens
+//    x 8 query heads of the GQA group, K via ldmatrix), the online softmax in fp32 (warp
+//    shuffles over the 8 lanes that share a query head), and O^T += V^T P^T (V^T via
 //    ldmatrix.trans, P^T transposed in registers with movmatrix). Each KV tile read from
 //    shared memory serves all G query heads of its group.
-//  * At a sequence boundary the four warps merge their (max, sum, O) states through shared
-//    memory and write the bf16 output, or an fp32 partial for the cross-CTA merge.
+//  * A sequence that lies inside one warp's range is finished from registers. A sequence
+//    cut by range boundaries leaves an fp32 partial (O, running max, running sum) per warp
+//    in the workspace; the last of those warps to finish (atomic counter) merges them.
 #include "common.cuh"
 
 namespace {
 
 using namespace b2p;
 
-constexpr int kConsumerWarps = 4;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kSub = 16;  // slots per sub-block = tokens per MMA tile
 
 struct DecodeParams {
@@ -52,235 +50,277 @@ struct DecodeParams {
   int block_size;  // multiple of 16
   int64_t num_blocks;
   float scale_log2;  // softmax scale * log2(e)
-  float* partials;   // [num_kv_heads][gridDim.x][2][NT*8*(D+2)]
+  float* partials;   // [num_kv_heads][units][2][record]
   int32_t* counters; // [num_kv_heads][num_seqs], zero between launches
   int32_t* err;
 };
 
-// Shared-memory plan (dynamic, 1024-byte aligned base).
-template <int D, int NT, int NS>
-struct Smem {
-  // Stage s is only ever consumed by warp s % kConsumerWarps, one use after another, so a
-  // consumer can never wait on a stage's phase u while phase u-1 is still pending (the
-  // parity of an mbarrier wait cannot tell those two apart).
-  static_assert(NS % kConsumerWarps == 0, "stages must be a multiple of the consumer warps");
-  static constexpr int kTileBytes = kSub * D * 2;  // one K or V sub-block of one head
-  static constexpr int kStageBytes = 2 * kTileBytes;
-  static constexpr int kStages = NS * kStageBytes;
-  static constexpr int kCombO = kConsumerWarps * NT * 8 * D * 4;  // fp32 O^T per warp
-  static constexpr int kCombML = kConsumerWarps * NT * 8 * 2 * 4;
-  static constexpr int kOffComb = kStages;
-  static constexpr int kOffML = kOffComb + kCombO;
-  static constexpr int kOffBar = kOffML + kCombML;
-  static constexpr int kOffMisc = kOffBar + 2 * NS * 8;
-  static constexpr int kTotal = kOffMisc + 8 * 8;
+template <int D, int NT>
+struct Record {
+  // fp32 O^T in MMA fragment order ([D/16][NT][32 lanes][4]), then max and sum per query
+  // head, so that a warp writes and reads its partial with coalesced 16-byte accesses.
+  static constexpr int kO = (D / 16) * NT * 32 * 4;
+  static constexpr int kFloats = kO + 2 * NT * 8;
 };
 
-struct CtaRange {
-  int64_t begin, end;  // global sub-block indices of this CTA (per KV head)
+struct Range {
+  int64_t begin, end;  // global sub-block indices of this unit (per KV head)
   int seq0;            // sequence containing `begin`
   int64_t cb0;         // first global sub-block index of seq0
   int64_t total;       // sub-blocks over all sequences (per KV head)
-  int64_t parts;       // ranges actually used: min(gridDim.x, total)
+  int64_t parts;       // ranges actually used: min(requested, total)
 };
 
 __device__ __forceinline__ int64_t range_start(int64_t c, int64_t total, int64_t parts) {
   return (c * total) / parts;
 }
 
-__device__ __forceinline__ int64_t owner_cta(int64_t b, int64_t total, int64_t parts) {
+__device__ __forceinline__ int64_t owner_unit(int64_t b, int64_t total, int64_t parts) {
   return ((b + 1) * parts - 1) / total;
 }
 
 __device__ __forceinline__ int sub_blocks_of(int ctx) { return ctx > 0 ? (ctx + kSub - 1) / kSub : 0; }
 
-// One warp: total sub-blocks over all sequences, then the sequence holding `target`.
-// Leaves the answer in lane 0's return value (all lanes return the same).
-__device__ void find_range(const DecodeParams& p, int64_t parts, int64_t c, CtaRange& r) {
+// One warp: total sub-blocks over all sequences, then the sequence holding unit c's first
+// sub-block. Each lane owns kPer consecutive sequences of a 32*kPer chunk and issues all
+// its loads before any arithmetic, so a batch of up to 256 sequences costs one memory
+// round trip; the second pass reuses the registers in that case.
+__device__ void find_range(const DecodeParams& p, int64_t parts, int64_t c, Range& r) {
+  constexpr int kPer = 8;
+  constexpr int kChunk = 32 * kPer;
   const int lane = threadIdx.x & 31;
+  int nbv[kPer];
   int64_t total = 0;
-  for (int base = 0; base < p.num_seqs; base += 32) {
-    const int i = base + lane;
-    int nb = 0;
-    if (i < p.num_seqs) nb = sub_blocks_of(__ldg(p.context_lens + i));
-    total += __reduce_add_sync(0xffffffffu, (unsigned)nb);
+  for (int base = 0; base < p.num_seqs; base += kChunk) {
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int i = base + lane * kPer + j;
+      nbv[j] = i < p.num_seqs ? __ldg(p.context_lens + i) : 0;
+    }
+    int sum = 0;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      nbv[j] = sub_blocks_of(nbv[j]);
+      sum += nbv[j];
+    }
+    total += __reduce_add_sync(0xffffffffu, (unsigned)sum);
   }
   r.total = total;
-  // Never more ranges than sub-blocks, so every range is non-empty and the CTAs that
+  // Never more ranges than sub-blocks, so every range is non-empty and the units that
   // share a sequence are exactly owner(first block) .. owner(last block).
   r.parts = parts < total ? parts : total;
+  r.seq0 = p.num_seqs;
+  r.cb0 = total;
   if (c >= r.parts) {
     r.begin = r.end = 0;
     return;
   }
   r.begin = range_start(c, total, r.parts);
   r.end = range_start(c + 1, total, r.parts);
-  r.seq0 = p.num_seqs;
-  r.cb0 = total;
-  if (r.begin >= r.end) return;
   int64_t run = 0;
-  for (int base = 0; base < p.num_seqs; base += 32) {
-    const int i = base + lane;
-    int nb = 0;
-    if (i < p.num_seqs) nb = sub_blocks_of(__ldg(p.context_lens + i));
-    // inclusive warp scan
-    int incl = nb;
+  for (int base = 0; base < p.num_seqs; base += kChunk) {
+    if (p.num_seqs > kChunk) {  // registers hold the last chunk only: reload this one
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int i = base + lane * kPer + j;
+        nbv[j] = sub_blocks_of(i < p.num_seqs ? __ldg(p.context_lens + i) : 0);
+      }
+    }
+    int sum = 0;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) sum += nbv[j];
+    int incl = sum;  // inclusive scan of per-lane sums
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int v = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += v;
     }
-    const int64_t hi = run + incl;  // exclusive end of sequence i
-    const unsigned hit = __ballot_sync(0xffffffffu, i < p.num_seqs && hi > r.begin);
+    const int64_t lane_lo = run + incl - sum;
+    const unsigned hit = __ballot_sync(0xffffffffu, run + incl > r.begin);
     if (hit) {
       const int src = __ffs(hit) - 1;
-      r.seq0 = base + src;
-      r.cb0 = run + __shfl_sync(0xffffffffu, incl - nb, src);
+      if (lane == src) {
+        int64_t cb = lane_lo;
+        int k = 0;
+        while (k < kPer - 1 && cb + nbv[k] <= r.begin) cb += nbv[k++];
+        r.seq0 = base + lane * kPer + k;
+        r.cb0 = cb;
+      }
+      r.seq0 = __shfl_sync(0xffffffffu, r.seq0, src);
+      r.cb0 = __shfl_sync(0xffffffffu, r.cb0, src);
       return;
     }
     run += __shfl_sync(0xffffffffu, incl, 31);
   }
 }
 
-template <typename T, int D, int NT, int NS>
-__global__ void __launch_bounds__(kThreads) paged_decode_tc(const __grid_constant__ CUtensorMap kmap,
-                                                            const __grid_constant__ CUtensorMap vmap,
-                                                            const DecodeParams p) {
-  using S = Smem<D, NT, NS>;
+// Maps a warp's consecutive sub-blocks to pool slot coordinates, 32 at a time: lane j
+// resolves sub-block (chunk0 + j) of the range. Sequences are found by a scan over windows
+// of 32 context lengths plus a per-lane binary search, then every lane reads its block
+// id; all loads of one call are independent of each other.
+struct SlotResolver {
+  int win_seq;     // first sequence that can hold the next chunk
+  int64_t win_cb;  // its first sub-block
+  int64_t begin, n;
+
+  __device__ int64_t operator()(const DecodeParams& p, int64_t chunk0, int lane,
+                                int64_t num_slots) {
+    const unsigned full_mask = 0xffffffffu;
+    const int spb = p.block_size / kSub;
+    const int64_t g = begin + chunk0 + lane;
+    const bool valid = chunk0 + lane < n;
+    int my_seq = -1;
+    int64_t my_cb = 0;
+    for (int guard = 0; guard < 1024; ++guard) {  // windows of 32 sequences
+      const int si = win_seq + lane;
+      const int nbj = si < p.num_seqs ? sub_blocks_of(__ldg(p.context_lens + si)) : 0;
+      int incl = nbj;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(full_mask, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const int64_t endj = win_cb + incl;  // exclusive end of sequence win_seq + lane
+      int lo = 0, hi = 32;  // smallest j with end_j > g
+#pragma unroll
+      for (int step = 0; step < 6; ++step) {
+        const int mid = (lo + hi) >> 1;
+        const int64_t e = __shfl_sync(full_mask, endj, mid < 32 ? mid : 31);
+        if (lo < hi) {
+          if (e > g) hi = mid; else lo = mid + 1;
+        }
+      }
+      const int64_t start_lo = __shfl_sync(full_mask, endj - nbj, lo < 32 ? lo : 31);
+      if (valid && my_seq < 0 && lo < 32) {
+        my_seq = win_seq + lo;
+        my_cb = start_lo;
+      }
+      if (!__any_sync(full_mask, valid && my_seq < 0)) break;
+      win_cb = __shfl_sync(full_mask, endj, 31);
+      win_seq += 32;
+      if (win_seq >= p.num_seqs) break;
+    }
+    // The next chunk starts in the sequence of this chunk's last sub-block.
+    const unsigned vmask = __ballot_sync(full_mask, valid && my_seq >= 0);
+    if (vmask) {
+      const int last = 31 - __clz(vmask);
+      win_seq = __shfl_sync(full_mask, my_seq, last);
+      win_cb = __shfl_sync(full_mask, my_cb, last);
+    }
+    if (!valid) return -1;
+    if (my_seq < 0) {
+      set_device_error(p.err, B2P_DEV_LENGTH);
+      return num_slots;
+    }
+    const int lb = (int)(g - my_cb);
+    const int64_t col = lb / spb;
+    const int32_t blk =
+        col < p.bt_stride ? __ldg(p.block_tables + (int64_t)my_seq * p.bt_stride + col) : -1;
+    if (blk < 0 || (int64_t)blk >= p.num_blocks) {
+      set_device_error(p.err, B2P_DEV_BLOCK_RANGE);
+      return num_slots;  // fully out of bounds: the TMA unit zero-fills the tile
+    }
+    return (int64_t)blk * p.block_size + (int64_t)(lb % spb) * kSub;
+  }
+};
+
+template <typename T, int D, int NT, int S, int W>
+__global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant__ CUtensorMap kmap,
+                                                          const __grid_constant__ CUtensorMap vmap,
+                                                          const DecodeParams p) {
+  constexpr int kTileBytes = kSub * D * 2;  // one K or V sub-block of one head
+  constexpr int kStageBytes = 2 * kTileBytes;
+  using Rec = Record<D, NT>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kOffBar);
-  uint64_t* empty = full + NS;
-  int64_t* misc = reinterpret_cast<int64_t*>(smem + S::kOffMisc);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 4);
-
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int head = blockIdx.y;  // KV head
-  const int64_t cta = blockIdx.x;
+  uint8_t* ring = smem + (size_t)warp * S * kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)W * S * kStageBytes) + warp * S;
 
-  if (warp == kConsumerWarps) {
-    CtaRange r;
-    find_range(p, (int64_t)gridDim.x, cta, r);
+  Range r;
+  const int64_t unit = (int64_t)blockIdx.x * W + warp;
+  find_range(p, (int64_t)gridDim.x * W, unit, r);
+  if (r.begin >= r.end) return;
+  const int64_t n = r.end - r.begin;
+  const int64_t parts = r.parts;
+  const int64_t num_slots = p.num_blocks * p.block_size;
+
+  if (lane == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&kmap);
+    tma_prefetch_desc(&vmap);
+  }
+  __syncwarp();
+
+  SlotResolver res{r.seq0, r.cb0, r.begin, n};
+  int64_t buf_base = 0;  // items [buf_base, buf_base + 32) are in slot_lo
+  int64_t slot_lo = res(p, 0, lane, num_slots);
+  int64_t slot_hi = n > 32 ? res(p, 32, lane, num_slots) : -1;
+  int64_t issued = 0;
+  bool aborted = false;
+
+  // Issue item k into stage k % S (all lanes call it; lane 0 issues the copies).
+  auto issue = [&](int64_t k) {
+    if (k >= buf_base + 32) {  // every item below k is issued: rotate the slot buffers
+      buf_base += 32;
+      slot_lo = slot_hi;
+      slot_hi = buf_base + 32 < n ? res(p, buf_base + 32, lane, num_slots) : -1;
+    }
+    const int64_t slot = __shfl_sync(0xffffffffu, slot_lo, (int)(k - buf_base));
     if (lane == 0) {
-      misc[0] = r.begin;
-      misc[1] = r.end;
-      misc[2] = r.seq0;
-      misc[3] = r.cb0;
-      misc[6] = r.total;
-      misc[7] = r.parts;
-      *abort_flag = 0;
-      for (int s = 0; s < NS; ++s) {
-        mbar_init(&full[s], 1);
-        mbar_init(&empty[s], 1);
-      }
-      fence_mbar_init();
-      tma_prefetch_desc(&kmap);
-      tma_prefetch_desc(&vmap);
+      const int stage = (int)(k % S);
+      uint8_t* kdst = ring + stage * kStageBytes;
+      const int c3 = (int)(slot < 0 ? num_slots : slot);
+      mbar_arrive_expect_tx(&full[stage], kStageBytes);
+      tma_load_5d(kdst, &kmap, &full[stage], 0, 0, head, c3, p.layer);
+      tma_load_5d(kdst + kTileBytes, &vmap, &full[stage], 0, 0, head, c3, p.layer);
     }
-  }
-  __syncthreads();
-  const int64_t begin = misc[0];
-  const int64_t end = misc[1];
-  if (begin >= end) return;
-  const int64_t nloc = end - begin;
-  const int64_t parts = misc[7];
+    issued = k + 1;
+  };
+  for (int64_t k = 0; k < S && k < n; ++k) issue(k);
 
-  // ------------------------------------------------------------------ producer
-  if (warp == kConsumerWarps) {
-    if (lane != 0) return;
-    int seq = (int)misc[2];
-    int64_t cb = misc[3];
-    int ctx = __ldg(p.context_lens + seq);
-    int nb = sub_blocks_of(ctx);
-    const int sub_per_block = p.block_size / kSub;
-    const int64_t num_slots = p.num_blocks * p.block_size;
-    int64_t issued = 0;
-    for (int64_t l = 0; l < nloc; ++l) {
-      const int64_t g = begin + l;
-      while (g >= cb + nb) {  // advance to the sequence holding g
-        cb += nb;
-        ++seq;
-        ctx = __ldg(p.context_lens + seq);
-        nb = sub_blocks_of(ctx);
-      }
-      const int stage = (int)(l % NS);
-      if (l >= NS) {
-        if (!mbar_wait_bounded(&empty[stage], (uint32_t)(((l / NS) - 1) & 1), p.err)) {
-          *abort_flag = 1;
-          break;
-        }
-      }
-      if (*abort_flag) break;
-      const int lb = (int)(g - cb);
-      const int64_t col = lb / sub_per_block;
-      const int32_t blk =
-          col < p.bt_stride ? __ldg(p.block_tables + (int64_t)seq * p.bt_stride + col) : -1;
-      int64_t slot = (int64_t)blk * p.block_size + (int64_t)(lb % sub_per_block) * kSub;
-      if (blk < 0 || (int64_t)blk >= p.num_blocks) {
-        set_device_error(p.err, B2P_DEV_BLOCK_RANGE);
-        slot = num_slots;  // fully out of bounds: the TMA unit zero-fills the tile
-      }
-      uint8_t* kdst = smem + stage * S::kStageBytes;
-      uint8_t* vdst = kdst + S::kTileBytes;
-      mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
-      tma_load_5d(kdst, &kmap, &full[stage], 0, 0, head, (int)slot, p.layer);
-      tma_load_5d(vdst, &vmap, &full[stage], 0, 0, head, (int)slot, p.layer);
-      issued = l + 1;
-    }
-    // Drain: never leave the CTA while TMA writes into its shared memory are in flight.
-    for (int64_t l = (issued > NS ? issued - NS : 0); l < issued; ++l) {
-      mbar_wait_bounded(&full[l % NS], (uint32_t)((l / NS) & 1), nullptr);
-    }
-    return;
-  }
-
-  // ------------------------------------------------------------------ consumers
   const int g8 = lane >> 2;  // row group (0..7)
   const int t4 = lane & 3;   // thread in group (0..3)
-  const int ctid = threadIdx.x;  // 0..127
-  float* combO = reinterpret_cast<float*>(smem + S::kOffComb);
-  float* combM = reinterpret_cast<float*>(smem + S::kOffML);
-  float* combL = combM + kConsumerWarps * NT * 8;
-  volatile int* merge_flag = reinterpret_cast<volatile int*>(misc + 5);
+  int seq = r.seq0;
+  int64_t cb = r.cb0;
+  int64_t gidx = r.begin;
+  int64_t k = 0;  // local item index
 
-  int seq = (int)misc[2];
-  int64_t cb = misc[3];
-  int64_t g = begin;
-  const size_t part_stride = (size_t)NT * 8 * (D + 2);
-
-  while (g < end) {
+  while (gidx < r.end) {
     const int ctx = __ldg(p.context_lens + seq);
     const int nb = sub_blocks_of(ctx);
-    const int lb0 = (int)(g - cb);
-    const int64_t seg_end_g = min(end, cb + nb);
-    const int lb1 = (int)(seg_end_g - cb);
     if (nb == 0) {
       // A decode sequence always has at least its own token; an empty history has no
       // softmax. Write zeros and flag it.
-      if (ctid == 0) set_device_error(p.err, B2P_DEV_LENGTH);
-      for (int e = ctid; e < p.group * D; e += kConsumerWarps * 32) {
+      if (lane == 0) set_device_error(p.err, B2P_DEV_LENGTH);
+      for (int e = lane; e < p.group * D; e += 32) {
         const int qh = e / D, d = e - qh * D;
-        reinterpret_cast<T*>(p.out)[(int64_t)seq * p.o_tok + (int64_t)(head * p.group + qh) * p.o_head + d] =
-            from_f32<T>(0.f);
+        reinterpret_cast<T*>(p.out)[(int64_t)seq * p.o_tok +
+                                    (int64_t)(head * p.group + qh) * p.o_head + d] = from_f32<T>(0.f);
       }
       ++seq;
       continue;
     }
+    const int lb0 = (int)(gidx - cb);
+    const int64_t seg_end = min(r.end, cb + nb);
+    const int lb1 = (int)(seg_end - cb);
 
     // Q fragments (B operand of S^T = K Q^T): Q[qh = g8 + 8n][16kk + 2t4 (+8)].
     uint32_t qf[NT][D / 16][2];
 #pragma unroll
-    for (int n = 0; n < NT; ++n) {
-      const int qh = n * 8 + g8;
+    for (int nn = 0; nn < NT; ++nn) {
+      const int qh = nn * 8 + g8;
       const bool ok = qh < p.group;
       const T* qrow = reinterpret_cast<const T*>(p.q) + (int64_t)seq * p.q_tok +
                       (int64_t)(head * p.group + (ok ? qh : 0)) * p.q_head;
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
-        qf[n][kk][0] = ok ? __ldg(reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * t4)) : 0u;
-        qf[n][kk][1] =
+        qf[nn][kk][0] = ok ? __ldg(reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * t4)) : 0u;
+        qf[nn][kk][1] =
             ok ? __ldg(reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 8 + 2 * t4)) : 0u;
       }
     }
@@ -288,29 +328,23 @@ __global__ void __launch_bounds__(kThreads) paged_decode_tc(const __grid_constan
     float m_run[NT][2], l_run[NT][2];
     float acc[D / 16][NT][4];
 #pragma unroll
-    for (int n = 0; n < NT; ++n) {
-      m_run[n][0] = m_run[n][1] = -INFINITY;
-      l_run[n][0] = l_run[n][1] = 0.f;
+    for (int nn = 0; nn < NT; ++nn) {
+      m_run[nn][0] = m_run[nn][1] = -INFINITY;
+      l_run[nn][0] = l_run[nn][1] = 0.f;
     }
 #pragma unroll
     for (int i = 0; i < D / 16; ++i)
 #pragma unroll
-      for (int n = 0; n < NT; ++n) acc[i][n][0] = acc[i][n][1] = acc[i][n][2] = acc[i][n][3] = 0.f;
+      for (int nn = 0; nn < NT; ++nn) acc[i][nn][0] = acc[i][nn][1] = acc[i][nn][2] = acc[i][nn][3] = 0.f;
 
-    // First local index in this segment that belongs to this warp.
-    const int64_t l_first = (cb + lb0) - begin;
-    int64_t l = l_first + ((warp - (int)(l_first % kConsumerWarps) + kConsumerWarps) % kConsumerWarps);
-    const int64_t l_last = (cb + lb1) - begin;  // exclusive
-    for (; l < l_last; l += kConsumerWarps) {
-      const int stage = (int)(l % NS);
-      if (*abort_flag) break;
-      if (!mbar_wait_bounded(&full[stage], (uint32_t)((l / NS) & 1), p.err)) {
-        *abort_flag = 1;
-        break;
-      }
-      const uint8_t* ktile = smem + stage * S::kStageBytes;
-      uint8_t* vtile = const_cast<uint8_t*>(ktile) + S::kTileBytes;
-      const int lb = (int)(begin + l - cb);
+    for (int lb = lb0; lb < lb1; ++lb, ++k) {
+      const int stage = (int)(k % S);
+      if (!aborted && !mbar_wait_bounded(&full[stage], (uint32_t)((k / S) & 1), p.err))
+        aborted = true;
+      aborted = __any_sync(0xffffffffu, aborted);
+      if (aborted) continue;  // keep walking so every sequence still gets written
+      uint8_t* ktile = ring + stage * kStageBytes;
+      uint8_t* vtile = ktile + kTileBytes;
       const int valid = min(kSub, ctx - lb * kSub);
       if (valid < kSub) {
         // Slots past the context may hold anything (the pool is not cleared), and
@@ -324,13 +358,17 @@ __global__ void __launch_bounds__(kThreads) paged_decode_tc(const __grid_constan
       const uint32_t kbase = smem_u32(ktile);
       const uint32_t vbase = smem_u32(vtile);
 
-      // ---- S^T = K Q^T  (M = 16 tokens, N = 8 query heads per tile, K = D)
-      float s[NT][4];
+      // ---- S^T = K Q^T  (M = 16 tokens, N = 8 query heads per tile, K = D); two
+      // accumulator sets (even / odd k-steps) halve the dependent MMA chain.
+      float s[NT][4], s2[NT][4];
 #pragma unroll
-      for (int n = 0; n < NT; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+      for (int nn = 0; nn < NT; ++nn) {
+        s[nn][0] = s[nn][1] = s[nn][2] = s[nn][3] = 0.f;
+        s2[nn][0] = s2[nn][1] = s2[nn][2] = s2[nn][3] = 0.f;
+      }
       {
-        const int mat = lane >> 3, r = lane & 7;
-        const int tok = r + (mat & 1) * 8;
+        const int mat = lane >> 3, rr = lane & 7;
+        const int tok = rr + (mat & 1) * 8;
         const int dsub = (mat >> 1) * 8;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -339,48 +377,53 @@ __global__ void __launch_bounds__(kThreads) paged_decode_tc(const __grid_constan
           uint32_t a0, a1, a2, a3;
           ldmatrix_x4(kbase + swz128(off), a0, a1, a2, a3);
 #pragma unroll
-          for (int n = 0; n < NT; ++n) MmaOp<T>::run(s[n], a0, a1, a2, a3, qf[n][kk][0], qf[n][kk][1]);
+          for (int nn = 0; nn < NT; ++nn)
+            MmaOp<T>::run((kk & 1) ? s2[nn] : s[nn], a0, a1, a2, a3, qf[nn][kk][0], qf[nn][kk][1]);
         }
+#pragma unroll
+        for (int nn = 0; nn < NT; ++nn)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) s[nn][e] += s2[nn][e];
       }
 
       // ---- online softmax over the tile's tokens (rows g8 and g8+8)
       const bool v0 = g8 < valid, v1 = g8 + 8 < valid;
       uint32_t pb[NT][2];
 #pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        float x0 = v0 ? s[n][0] * p.scale_log2 : -INFINITY;
-        float x1 = v0 ? s[n][1] * p.scale_log2 : -INFINITY;
-        float x2 = v1 ? s[n][2] * p.scale_log2 : -INFINITY;
-        float x3 = v1 ? s[n][3] * p.scale_log2 : -INFINITY;
+      for (int nn = 0; nn < NT; ++nn) {
+        const float x0 = v0 ? s[nn][0] * p.scale_log2 : -INFINITY;
+        const float x1 = v0 ? s[nn][1] * p.scale_log2 : -INFINITY;
+        const float x2 = v1 ? s[nn][2] * p.scale_log2 : -INFINITY;
+        const float x3 = v1 ? s[nn][3] * p.scale_log2 : -INFINITY;
         float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
 #pragma unroll
         for (int o = 4; o < 32; o <<= 1) {
           mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
           mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
         }
-        const float mn0 = fmaxf(m_run[n][0], mx0), mn1 = fmaxf(m_run[n][1], mx1);
-        const float al0 = fast_exp2(m_run[n][0] - mn0), al1 = fast_exp2(m_run[n][1] - mn1);
-        m_run[n][0] = mn0;
-        m_run[n][1] = mn1;
+        const float mn0 = fmaxf(m_run[nn][0], mx0), mn1 = fmaxf(m_run[nn][1], mx1);
+        const float al0 = fast_exp2(m_run[nn][0] - mn0), al1 = fast_exp2(m_run[nn][1] - mn1);
+        m_run[nn][0] = mn0;
+        m_run[nn][1] = mn1;
         const float p0 = fast_exp2(x0 - mn0), p1 = fast_exp2(x1 - mn1);
         const float p2 = fast_exp2(x2 - mn0), p3 = fast_exp2(x3 - mn1);
-        l_run[n][0] = l_run[n][0] * al0 + p0 + p2;
-        l_run[n][1] = l_run[n][1] * al1 + p1 + p3;
+        l_run[nn][0] = l_run[nn][0] * al0 + p0 + p2;
+        l_run[nn][1] = l_run[nn][1] * al1 + p1 + p3;
 #pragma unroll
         for (int i = 0; i < D / 16; ++i) {
-          acc[i][n][0] *= al0;
-          acc[i][n][1] *= al1;
-          acc[i][n][2] *= al0;
-          acc[i][n][3] *= al1;
+          acc[i][nn][0] *= al0;
+          acc[i][nn][1] *= al1;
+          acc[i][nn][2] *= al0;
+          acc[i][nn][3] *= al1;
         }
-        pb[n][0] = movmatrix_trans(pack2<T>(p0, p1));
-        pb[n][1] = movmatrix_trans(pack2<T>(p2, p3));
+        pb[nn][0] = movmatrix_trans(pack2<T>(p0, p1));
+        pb[nn][1] = movmatrix_trans(pack2<T>(p2, p3));
       }
 
       // ---- O^T += V^T P^T  (M = 16 dims per tile, N = 8 query heads, K = 16 tokens)
       {
-        const int mat = lane >> 3, r = lane & 7;
-        const int tok = r + (mat >> 1) * 8;
+        const int mat = lane >> 3, rr = lane & 7;
+        const int tok = rr + (mat >> 1) * 8;
         const int dsub = (mat & 1) * 8;
 #pragma unroll
         for (int i = 0; i < D / 16; ++i) {
@@ -389,122 +432,136 @@ __global__ void __launch_bounds__(kThreads) paged_decode_tc(const __grid_constan
           uint32_t a0, a1, a2, a3;
           ldmatrix_x4_trans(vbase + swz128(off), a0, a1, a2, a3);
 #pragma unroll
-          for (int n = 0; n < NT; ++n) MmaOp<T>::run(acc[i][n], a0, a1, a2, a3, pb[n][0], pb[n][1]);
+          for (int nn = 0; nn < NT; ++nn)
+            MmaOp<T>::run(acc[i][nn], a0, a1, a2, a3, pb[nn][0], pb[nn][1]);
         }
       }
-      if (valid < kSub) fence_proxy_async_smem();  // generic writes before the TMA reuses it
+      // Refill this stage with the item S ahead. All reads of the stage are complete (their
+      // results fed the MMAs above); generic writes (the zeroed rows) need a proxy fence
+      // before the TMA unit writes the same bytes.
+      if (valid < kSub) fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[stage]);
+      if (k + S < n) issue(k + S);
     }
 
-    // ---- merge the four warps' states for this segment
+    // ---- finish the segment: full sums per query head
 #pragma unroll
-    for (int n = 0; n < NT; ++n) {
+    for (int nn = 0; nn < NT; ++nn) {
 #pragma unroll
       for (int o = 4; o < 32; o <<= 1) {
-        l_run[n][0] += __shfl_xor_sync(0xffffffffu, l_run[n][0], o);
-        l_run[n][1] += __shfl_xor_sync(0xffffffffu, l_run[n][1], o);
-      }
-      if (g8 == 0) {
-        combM[(warp * NT + n) * 8 + 2 * t4] = m_run[n][0];
-        combM[(warp * NT + n) * 8 + 2 * t4 + 1] = m_run[n][1];
-        combL[(warp * NT + n) * 8 + 2 * t4] = l_run[n][0];
-        combL[(warp * NT + n) * 8 + 2 * t4 + 1] = l_run[n][1];
-      }
-#pragma unroll
-      for (int i = 0; i < D / 16; ++i) {
-        float* base = combO + (size_t)(warp * NT + n) * 8 * D;
-        base[(2 * t4) * D + i * 16 + g8] = acc[i][n][0];
-        base[(2 * t4 + 1) * D + i * 16 + g8] = acc[i][n][1];
-        base[(2 * t4) * D + i * 16 + g8 + 8] = acc[i][n][2];
-        base[(2 * t4 + 1) * D + i * 16 + g8 + 8] = acc[i][n][3];
+        l_run[nn][0] += __shfl_xor_sync(0xffffffffu, l_run[nn][0], o);
+        l_run[nn][1] += __shfl_xor_sync(0xffffffffu, l_run[nn][1], o);
       }
     }
-    asm volatile("bar.sync 1, %0;\n" ::"r"(kConsumerWarps * 32) : "memory");
-
     const bool complete = (lb0 == 0) && (lb1 == nb);
-    const int nelem = p.group * D;
-    float* part = nullptr;
-    if (!complete) {
-      const int slot_idx = (cb + lb0 == begin) ? 0 : 1;  // first segment of this CTA or not
-      part = p.partials + (((size_t)head * parts + cta) * 2 + slot_idx) * part_stride;
-    }
-    for (int e = ctid; e < nelem; e += kConsumerWarps * 32) {
-      const int qh = e / D, d = e - qh * D;
-      const int n = qh >> 3, col = qh & 7;
-      float M = -INFINITY;
+    auto write_out = [&](float (&o)[D / 16][NT][4], float (&lsum)[NT][2]) {
 #pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, combM[(w * NT + n) * 8 + col]);
-      float L = 0.f, O = 0.f;
+      for (int nn = 0; nn < NT; ++nn) {
 #pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) {
-        const float sc = fast_exp2(combM[(w * NT + n) * 8 + col] - M);
-        L += combL[(w * NT + n) * 8 + col] * sc;
-        O += combO[(size_t)(w * NT + n) * 8 * D + col * D + d] * sc;
-      }
-      if (complete) {
-        T* orow = reinterpret_cast<T*>(p.out) + (int64_t)seq * p.o_tok +
-                  (int64_t)(head * p.group + qh) * p.o_head;
-        orow[d] = from_f32<T>(O / L);
-      } else {
-        part[qh * D + d] = O;
-        if (d == 0) {
-          part[NT * 8 * D + qh] = M;
-          part[NT * 8 * D + NT * 8 + qh] = L;
-        }
-      }
-    }
-
-    if (!complete) {
-      __threadfence();
-      asm volatile("bar.sync 1, %0;\n" ::"r"(kConsumerWarps * 32) : "memory");
-      if (ctid == 0) {
-        const int64_t tot = misc[6];
-        const int64_t c_first = owner_cta(cb, tot, parts);
-        const int64_t c_last = owner_cta(cb + nb - 1, tot, parts);
-        const int expected = (int)(c_last - c_first + 1);
-        int32_t* ctr = p.counters + (size_t)head * p.num_seqs + seq;
-        const int prev = atomicAdd(ctr, 1);
-        const int last = (prev == expected - 1);
-        if (last) *ctr = 0;  // leave the workspace zeroed for the next launch
-        *merge_flag = last;
-      }
-      asm volatile("bar.sync 1, %0;\n" ::"r"(kConsumerWarps * 32) : "memory");
-      if (*merge_flag) {
-        __threadfence();
-        const int64_t tot = misc[6];
-        const int64_t c_first = owner_cta(cb, tot, parts);
-        const int64_t c_last = owner_cta(cb + nb - 1, tot, parts);
-        for (int e = ctid; e < nelem; e += kConsumerWarps * 32) {
-          const int qh = e / D, d = e - qh * D;
-          float M = -INFINITY;
-          for (int64_t c = c_first; c <= c_last; ++c) {
-            const int si = (c == c_first && range_start(c, tot, parts) != cb) ? 1 : 0;
-            const float* pc = p.partials + (((size_t)head * parts + c) * 2 + si) * part_stride;
-            M = fmaxf(M, __ldcg(pc + NT * 8 * D + qh));
-          }
-          float L = 0.f, O = 0.f;
-          for (int64_t c = c_first; c <= c_last; ++c) {
-            const int si = (c == c_first && range_start(c, tot, parts) != cb) ? 1 : 0;
-            const float* pc = p.partials + (((size_t)head * parts + c) * 2 + si) * part_stride;
-            const float sc = fast_exp2(__ldcg(pc + NT * 8 * D + qh) - M);
-            L += __ldcg(pc + NT * 8 * D + NT * 8 + qh) * sc;
-            O += __ldcg(pc + qh * D + d) * sc;
-          }
+        for (int cc = 0; cc < 2; ++cc) {
+          const int qh = nn * 8 + 2 * t4 + cc;
+          if (qh >= p.group) continue;
+          const float inv = lsum[nn][cc] > 0.f ? 1.f / lsum[nn][cc] : 0.f;
           T* orow = reinterpret_cast<T*>(p.out) + (int64_t)seq * p.o_tok +
                     (int64_t)(head * p.group + qh) * p.o_head;
-          orow[d] = from_f32<T>(O / L);
+#pragma unroll
+          for (int i = 0; i < D / 16; ++i) {
+            orow[i * 16 + g8] = from_f32<T>(o[i][nn][cc] * inv);
+            orow[i * 16 + g8 + 8] = from_f32<T>(o[i][nn][2 + cc] * inv);
+          }
         }
       }
+    };
+    if (complete) {
+      write_out(acc, l_run);
+    } else {
+      const int slot_idx = (cb + lb0 == r.begin) ? 0 : 1;  // first segment of this unit or not
+      float* rec = p.partials + (((size_t)head * parts + unit) * 2 + slot_idx) * Rec::kFloats;
+#pragma unroll
+      for (int i = 0; i < D / 16; ++i)
+#pragma unroll
+        for (int nn = 0; nn < NT; ++nn)
+          reinterpret_cast<float4*>(rec)[(i * NT + nn) * 32 + lane] =
+              make_float4(acc[i][nn][0], acc[i][nn][1], acc[i][nn][2], acc[i][nn][3]);
+      if (g8 == 0) {
+#pragma unroll
+        for (int nn = 0; nn < NT; ++nn) {
+          rec[Rec::kO + nn * 8 + 2 * t4] = m_run[nn][0];
+          rec[Rec::kO + nn * 8 + 2 * t4 + 1] = m_run[nn][1];
+          rec[Rec::kO + NT * 8 + nn * 8 + 2 * t4] = l_run[nn][0];
+          rec[Rec::kO + NT * 8 + nn * 8 + 2 * t4 + 1] = l_run[nn][1];
+        }
+      }
+      const int64_t u_first = owner_unit(cb, r.total, parts);
+      const int64_t u_last = owner_unit(cb + nb - 1, r.total, parts);
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) {
+        __threadfence();  // this warp's partial is visible before the count says so
+        int32_t* ctr = p.counters + (size_t)head * p.num_seqs + seq;
+        const int prev = atomicAdd(ctr, 1);
+        last = prev == (int)(u_last - u_first);
+        if (last) {
+          *ctr = 0;  // leave the workspace zeroed for the next launch
+          __threadfence();
+        }
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        // Merge every unit's partial of this sequence (this warp's own included), reading
+        // through L2: the other partials were written by other SMs.
+        float M[NT][2];
+#pragma unroll
+        for (int nn = 0; nn < NT; ++nn) M[nn][0] = M[nn][1] = -INFINITY;
+        for (int64_t u = u_first; u <= u_last; ++u) {
+          const int si = (u == u_first && range_start(u, r.total, parts) != cb) ? 1 : 0;
+          const float* pr = p.partials + (((size_t)head * parts + u) * 2 + si) * Rec::kFloats;
+#pragma unroll
+          for (int nn = 0; nn < NT; ++nn) {
+            M[nn][0] = fmaxf(M[nn][0], __ldcg(pr + Rec::kO + nn * 8 + 2 * t4));
+            M[nn][1] = fmaxf(M[nn][1], __ldcg(pr + Rec::kO + nn * 8 + 2 * t4 + 1));
+          }
+        }
+        float L[NT][2];
+#pragma unroll
+        for (int nn = 0; nn < NT; ++nn) {
+          L[nn][0] = L[nn][1] = 0.f;
+#pragma unroll
+          for (int i = 0; i < D / 16; ++i) acc[i][nn][0] = acc[i][nn][1] = acc[i][nn][2] = acc[i][nn][3] = 0.f;
+        }
+        for (int64_t u = u_first; u <= u_last; ++u) {
+          const int si = (u == u_first && range_start(u, r.total, parts) != cb) ? 1 : 0;
+          const float* pr = p.partials + (((size_t)head * parts + u) * 2 + si) * Rec::kFloats;
+#pragma unroll
+          for (int nn = 0; nn < NT; ++nn) {
+            const float sc0 = fast_exp2(__ldcg(pr + Rec::kO + nn * 8 + 2 * t4) - M[nn][0]);
+            const float sc1 = fast_exp2(__ldcg(pr + Rec::kO + nn * 8 + 2 * t4 + 1) - M[nn][1]);
+            L[nn][0] += __ldcg(pr + Rec::kO + NT * 8 + nn * 8 + 2 * t4) * sc0;
+            L[nn][1] += __ldcg(pr + Rec::kO + NT * 8 + nn * 8 + 2 * t4 + 1) * sc1;
+#pragma unroll
+            for (int i = 0; i < D / 16; ++i) {
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(pr) + (i * NT + nn) * 32 + lane);
+              acc[i][nn][0] += v.x * sc0;
+              acc[i][nn][1] += v.y * sc1;
+              acc[i][nn][2] += v.z * sc0;
+              acc[i][nn][3] += v.w * sc1;
+            }
+          }
+        }
+        write_out(acc, L);
+      }
     }
-    asm volatile("bar.sync 1, %0;\n" ::"r"(kConsumerWarps * 32) : "memory");
-    // After an abort the warps skip all waits and MMA work but still walk every segment,
-    // so the named barriers above are always reached by all four consumer warps.
-    g = seg_end_g;
+    gidx = seg_end;
     if (lb1 == nb) {
       cb += nb;
       ++seq;
     }
+  }
+  // Never leave while TMA writes into this warp's stages are in flight (only possible
+  // after an abort; otherwise every issued item has been waited for).
+  if (lane == 0) {
+    for (int64_t kk = k; kk < issued; ++kk)
+      mbar_wait_bounded(&full[kk % S], (uint32_t)((kk / S) & 1), nullptr);
   }
 }
 
@@ -513,44 +570,48 @@ __global__ void __launch_bounds__(kThreads) paged_decode_tc(const __grid_constan
 // ====================================================================== host side
 namespace {
 
-using KernelFn = void (*)(CUtensorMap, CUtensorMap, DecodeParams);
-
 struct Plan {
   const void* fn = nullptr;
   int smem = 0;
+  int warps = 0;        // W: stream units per CTA
+  int record = 0;       // floats per partial record
   int ctas_per_sm = 0;
 };
 
-template <typename T, int D, int NT, int NS>
+template <typename T, int D, int NT, int S, int W>
 Plan make_plan() {
   Plan pl;
-  pl.fn = reinterpret_cast<const void*>(&paged_decode_tc<T, D, NT, NS>);
-  pl.smem = Smem<D, NT, NS>::kTotal + 1024;  // + alignment slack for the 1024-byte base
+  pl.fn = reinterpret_cast<const void*>(&paged_decode_tc<T, D, NT, S, W>);
+  // W rings of S stages (K and V tile each), W*S mbarriers, + slack for the 1024 alignment.
+  pl.smem = W * S * (2 * kSub * D * 2) + W * S * 8 + 1024;
+  pl.warps = W;
+  pl.record = Record<D, NT>::kFloats;
   return pl;
 }
 
-// Pick the kernel instantiation for (dtype, head_dim, group). Stage counts keep roughly
-// 48-64 KiB of K/V tiles in flight per CTA.
+// Kernel instantiation for (dtype, head_dim, group). Each warp keeps S stages of K+V tiles
+// in flight; with 4 warps per CTA and three CTAs per SM (two for head_dim 256) that is
+// 96-192 KiB of HBM reads in flight per SM.
 bool select_plan(int dtype, int head_dim, int group, Plan& pl) {
   const int nt = group <= 8 ? 1 : (group <= 16 ? 2 : 0);
   if (nt == 0) return false;
-#define B2P_CASE(TT, DD, NN, SS)                                                  \
-  if (head_dim == DD && nt == NN) {                                               \
-    pl = make_plan<TT, DD, NN, SS>();                                             \
-    return true;                                                                  \
+#define B2P_CASE(TT, DD, NN, SS)                 \
+  if (head_dim == DD && nt == NN) {              \
+    pl = make_plan<TT, DD, NN, SS, 4>();         \
+    return true;                                 \
   }
   if (dtype == B2P_BF16) {
-    B2P_CASE(__nv_bfloat16, 64, 1, 12)
-    B2P_CASE(__nv_bfloat16, 64, 2, 12)
-    B2P_CASE(__nv_bfloat16, 128, 1, 8)
-    B2P_CASE(__nv_bfloat16, 128, 2, 8)
-    B2P_CASE(__nv_bfloat16, 256, 1, 4)
+    B2P_CASE(__nv_bfloat16, 64, 1, 4)
+    B2P_CASE(__nv_bfloat16, 64, 2, 4)
+    B2P_CASE(__nv_bfloat16, 128, 1, 2)
+    B2P_CASE(__nv_bfloat16, 128, 2, 2)
+    B2P_CASE(__nv_bfloat16, 256, 1, 2)
   } else if (dtype == B2P_F16) {
-    B2P_CASE(__half, 64, 1, 12)
-    B2P_CASE(__half, 64, 2, 12)
-    B2P_CASE(__half, 128, 1, 8)
-    B2P_CASE(__half, 128, 2, 8)
-    B2P_CASE(__half, 256, 1, 4)
+    B2P_CASE(__half, 64, 1, 4)
+    B2P_CASE(__half, 64, 2, 4)
+    B2P_CASE(__half, 128, 1, 2)
+    B2P_CASE(__half, 128, 2, 2)
+    B2P_CASE(__half, 256, 1, 2)
   }
 #undef B2P_CASE
   return false;
@@ -568,13 +629,13 @@ int prepare(Plan& pl) {
       return B2P_OK;
     }
   }
-  if (cudaFuncSetAttribute(pl.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem) !=
-      cudaSuccess)
-    return b2p_host::check_launch();
+  cudaError_t e = cudaFuncSetAttribute(pl.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
+  if (e != cudaSuccess) return b2p_host::record_error(e);
   int occ = 0;
-  cudaError_t oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, pl.fn, kThreads, pl.smem);
-  if (oe != cudaSuccess) return b2p_host::record_error(oe);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, pl.fn, pl.warps * 32, pl.smem);
+  if (e != cudaSuccess) return b2p_host::record_error(e);
   if (occ <= 0) return B2P_EUNSUPPORTED;
+  if (occ > 8) occ = 8;  // the workspace is sized for at most 8 CTAs per SM
   for (int i = 0; i < 16; ++i) {
     if (last_fn[i] == nullptr) {
       last_fn[i] = pl.fn;
@@ -587,17 +648,20 @@ int prepare(Plan& pl) {
   return B2P_OK;
 }
 
-int64_t parts_per_head(int ctas_per_sm, int num_kv_heads) {
-  if (ctas_per_sm > 8) ctas_per_sm = 8;  // the workspace is sized for at most 8 per SM
+// CTAs per KV head: one wave over all SMs.
+int64_t ctas_per_head(int ctas_per_sm, int num_kv_heads) {
   const int64_t slots = (int64_t)b2p_host::sm_count() * ctas_per_sm;
-  int64_t parts = slots / num_kv_heads;
-  return parts < 1 ? 1 : parts;
+  const int64_t c = slots / num_kv_heads;
+  return c < 1 ? 1 : c;
 }
 
-size_t workspace_bytes(int num_seqs, int num_kv_heads, int head_dim, int nt, int64_t parts) {
-  const size_t counters = ((size_t)num_kv_heads * num_seqs * 4 + 255) & ~size_t(255);
-  const size_t part = (size_t)num_kv_heads * parts * 2 * nt * 8 * (head_dim + 2) * 4;
-  return counters + part;
+size_t counters_bytes(int num_seqs, int num_kv_heads) {
+  return ((size_t)num_kv_heads * num_seqs * 4 + 255) & ~size_t(255);
+}
+
+size_t workspace_bytes(int num_seqs, int num_kv_heads, int64_t units, int record) {
+  return counters_bytes(num_seqs, num_kv_heads) +
+         (size_t)num_kv_heads * units * 2 * record * sizeof(float);
 }
 
 }  // namespace
@@ -606,9 +670,11 @@ extern "C" size_t b2p_paged_decode_workspace_size(int num_seqs, int num_q_heads,
                                                   int num_kv_heads, int head_dim) {
   if (num_seqs <= 0 || num_kv_heads <= 0 || num_q_heads <= 0 || head_dim <= 0) return 0;
   const int group = num_q_heads / num_kv_heads;
-  const int nt = group <= 8 ? 1 : 2;
-  // Upper bound over the instantiations: at most 8 CTAs of this kernel fit on an SM.
-  return workspace_bytes(num_seqs, num_kv_heads, head_dim, nt, parts_per_head(8, num_kv_heads));
+  Plan pl;
+  if (!select_plan(B2P_BF16, head_dim, group, pl)) return 16;  // CUDA-core path: none needed
+  // Upper bound over occupancies (at most 8 CTAs per SM are used).
+  const int64_t units = ctas_per_head(8, num_kv_heads) * pl.warps;
+  return workspace_bytes(num_seqs, num_kv_heads, units, pl.record);
 }
 
 int b2p_decode_simt(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
@@ -645,7 +711,7 @@ extern "C" int b2p_paged_decode(const void* q, int64_t q_tok_stride, int64_t q_h
                   ((reinterpret_cast<uintptr_t>(q) & 3u) == 0) &&
                   ((reinterpret_cast<uintptr_t>(key_cache) & 15u) == 0) &&
                   ((reinterpret_cast<uintptr_t>(value_cache) & 15u) == 0) &&
-                  select_plan(dtype, head_dim, group, pl);
+                  num_slots <= 0x7fffffffLL && select_plan(dtype, head_dim, group, pl);
   if (!tc) {
     return b2p_decode_simt(q, q_tok_stride, q_head_stride, key_cache, value_cache, layer_index,
                            num_layers, num_slots, block_tables, block_table_stride, context_lens,
@@ -655,9 +721,8 @@ extern "C" int b2p_paged_decode(const void* q, int64_t q_tok_stride, int64_t q_h
   if (!workspace) return B2P_EWORKSPACE;
   int rc = prepare(pl);
   if (rc != B2P_OK) return rc;
-  const int nt = group <= 8 ? 1 : 2;
-  const int64_t parts = parts_per_head(pl.ctas_per_sm, num_kv_heads);
-  const size_t need = workspace_bytes(num_seqs, num_kv_heads, head_dim, nt, parts);
+  const int64_t ctas = ctas_per_head(pl.ctas_per_sm, num_kv_heads);
+  const size_t need = workspace_bytes(num_seqs, num_kv_heads, ctas * pl.warps, pl.record);
   if (workspace_size < need) return B2P_EWORKSPACE;
 
   CUtensorMap kmap, vmap;
@@ -684,14 +749,14 @@ extern "C" int b2p_paged_decode(const void* q, int64_t q_tok_stride, int64_t q_h
   p.block_size = block_size;
   p.num_blocks = num_slots / block_size;
   p.scale_log2 = scale * kLog2e;
-  const size_t counters_bytes = ((size_t)num_kv_heads * num_seqs * 4 + 255) & ~size_t(255);
   p.counters = static_cast<int32_t*>(workspace);
-  p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + counters_bytes);
+  p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                        counters_bytes(num_seqs, num_kv_heads));
   p.err = err_flag;
 
-  dim3 grid((unsigned)parts, (unsigned)num_kv_heads);
+  dim3 grid((unsigned)ctas, (unsigned)num_kv_heads);
   void* args[] = {&kmap, &vmap, &p};
-  cudaError_t e = cudaLaunchKernel(pl.fn, grid, dim3(kThreads), args, (size_t)pl.smem,
+  cudaError_t e = cudaLaunchKernel(pl.fn, grid, dim3(pl.warps * 32), args, (size_t)pl.smem,
                                    static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return b2p_host::record_error(e);
   return b2p_host::check_launch();

@@ -1,0 +1,176 @@
+"""Continuous-batching scheduler (interface and policy of serving/engine/scheduler.py:12-458).
+
+Policy, which the slot mappings depend on and which therefore matches the reference:
+every running sequence decodes first (one budget token each); waiting sequences are then
+admitted first-come-first-served for whole-history prefill while the token budget, the
+concurrency limit and the free blocks allow, stopping at the first one that does not
+fit. When reserving a block for a generated token runs out of blocks, the most recently
+admitted other running sequence is preempted (blocks freed, put back at the head of the
+waiting queue) and re-prefilled later.
+"""
+
+from __future__ import annotations
+
+from collections import deque
+from dataclasses import dataclass
+
+from .block import BlockPool, BlockTable, blocks_needed
+from .config import EngineConfiguration
+from .request import Request
+from .sequence import FinishReason, SequenceState
+
+_NO_BLOCKS = "Not enough free blocks available"
+
+
+@dataclass(frozen=True)
+class SchedulerOutput:
+    decode_sequences: tuple[SequenceState, ...]
+    prefill_sequences: tuple[SequenceState, ...]
+    num_batched_tokens: int
+
+
+class Scheduler:
+    """Owns the request queues, the block pool and the block table of one replica."""
+
+    def __init__(self, configuration: EngineConfiguration) -> None:
+        self.configuration = configuration
+        self.block_pool = BlockPool(num_blocks=configuration.num_blocks)
+        self.block_table = BlockTable(pool=self.block_pool, block_size=configuration.block_size)
+        self._waiting: deque[SequenceState] = deque()
+        self._running: list[SequenceState] = []
+        self._finished: list[SequenceState] = []
+        self._ids: set[str] = set()
+        self._num_preemptions = 0
+
+    # ------------------------------------------------------------------ views
+    @property
+    def waiting_sequences(self) -> tuple[SequenceState, ...]:
+        return tuple(self._waiting)
+
+    @property
+    def running_sequences(self) -> tuple[SequenceState, ...]:
+        return tuple(self._running)
+
+    @property
+    def finished_sequences(self) -> tuple[SequenceState, ...]:
+        return tuple(self._finished)
+
+    @property
+    def num_preemptions(self) -> int:
+        return self._num_preemptions
+
+    @property
+    def has_unfinished_requests(self) -> bool:
+        return bool(self._waiting or self._running)
+
+    # ------------------------------------------------------------------ requests
+    def submit(self, request: Request) -> SequenceState:
+        if request.request_id in self._ids:
+            raise ValueError(f"request_id {request.request_id!r} has already been submitted.")
+        cfg = self.configuration
+        n = len(request.prompt_token_ids)
+        if n > cfg.max_batched_tokens:
+            raise ValueError("Prompt length exceeds max_batched_tokens and cannot be "
+                             "prefilled without chunked prefill.")
+        longest = n + request.max_new_tokens - 1  # the last token never needs a KV slot
+        if longest > cfg.max_batched_tokens:
+            raise ValueError("Maximum non-terminal sequence length exceeds max_batched_tokens "
+                             "and cannot be re-prefilled without chunked prefill.")
+        if blocks_needed(longest, cfg.block_size) > cfg.num_blocks:
+            raise ValueError("Maximum non-terminal sequence length requires more KV-cache "
+                             "blocks than the scheduler owns.")
+        seq = SequenceState(request=request)
+        self._waiting.append(seq)
+        self._ids.add(request.request_id)
+        return seq
+
+    def cancel(self, request_id: str) -> bool:
+        for seq in self._waiting:
+            if seq.request.request_id == request_id:
+                self._waiting.remove(seq)
+                seq.mark_finished(FinishReason.CANCELLED)
+                self._finished.append(seq)
+                return True
+        for seq in self._running:
+            if seq.request.request_id == request_id:
+                self._release(seq)
+                seq.mark_finished(FinishReason.CANCELLED)
+                self._finished.append(seq)
+                return True
+        return False
+
+    # ------------------------------------------------------------------ scheduling
+    def _fits(self, seq: SequenceState) -> bool:
+        if len(self._running) >= self.configuration.max_sequences:
+            return False
+        need = blocks_needed(seq.current_length, self.configuration.block_size)
+        return need <= self.block_pool.num_free_blocks
+
+    def _admit(self, seq: SequenceState) -> None:
+        if not self._waiting or self._waiting[0] is not seq:
+            raise RuntimeError("Admission violated waiting-queue ordering.")
+        self.block_table.allocate_for_request(seq.request.request_id, seq.current_length)
+        self._waiting.popleft()
+        seq.mark_running()
+        self._running.append(seq)
+
+    def schedule(self) -> SchedulerOutput:
+        budget = self.configuration.max_batched_tokens
+        decode = tuple(self._running)
+        budget -= len(decode)
+        prefill: list[SequenceState] = []
+        while self._waiting and budget > 0:
+            head = self._waiting[0]
+            need = head.current_length
+            if need > budget or not self._fits(head):
+                break
+            self._admit(head)
+            prefill.append(head)
+            budget -= need
+        tokens = len(decode) + sum(s.current_length for s in prefill)
+        return SchedulerOutput(decode_sequences=decode, prefill_sequences=tuple(prefill),
+                               num_batched_tokens=tokens)
+
+    def reserve_generated_token(self, sequence: SequenceState) -> None:
+        if sequence.is_finished:
+            raise RuntimeError("Cannot reserve KV-cache storage for a finished sequence.")
+        if not any(s is sequence for s in self._running):
+            raise RuntimeError(
+                "Cannot reserve KV-cache storage for a sequence that is not running.")
+        rid = sequence.request.request_id
+        try:
+            self.block_table.append_token(rid, sequence.current_length)
+            return
+        except RuntimeError as err:
+            if _NO_BLOCKS not in str(err):
+                raise
+        victim = next((s for s in reversed(self._running) if s is not sequence), None)
+        if victim is None:
+            raise RuntimeError(
+                "Not enough KV-cache capacity and no eligible preemption victim exists.")
+        self._preempt(victim)
+        self.block_table.append_token(rid, sequence.current_length)
+
+    def finish_sequence(self, sequence: SequenceState, reason: FinishReason) -> None:
+        if sequence.is_finished:
+            raise RuntimeError("Cannot finish a sequence that is already finished.")
+        if not any(s is sequence for s in self._running):
+            raise RuntimeError("Cannot finish a sequence that is not running.")
+        self._release(sequence)
+        sequence.mark_finished(reason)
+        self._finished.append(sequence)
+
+    # ------------------------------------------------------------------ internals
+    def _release(self, seq: SequenceState) -> None:
+        self.block_table.free_request(seq.request.request_id)
+        self._running = [s for s in self._running if s is not seq]
+
+    def _preempt(self, seq: SequenceState) -> None:
+        if seq.is_finished:
+            raise RuntimeError("Cannot preempt a finished sequence.")
+        if not any(s is seq for s in self._running):
+            raise RuntimeError("Cannot preempt a sequence that is not running.")
+        self._release(seq)
+        seq.mark_preempted()
+        self._waiting.appendleft(seq)
+        self._num_preemptions += 1

@@ -1,0 +1,124 @@
+"""CPU parity of the engine bookkeeping with traces recorded from the reference engine.
+
+tests/golden/engine_trace_*.json were produced by running the reference Engine,
+Scheduler and BlockPool (tests/golden/make_golden.py) with a deterministic stand-in model.
+Replaying the same requests through this package's engine must give the same executions
+at every step — request order, phase, length, block list, last slot and a checksum of the
+whole-history slot ids — the same preemption count and the same finished tokens.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from llm_engineering_b200 import engine as eng
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+class HashRunner:
+    """The stand-in model used when the traces were recorded."""
+
+    def __init__(self, vocab: int, eos: int | None = None, eos_every: int = 0):
+        self.vocab, self.eos, self.eos_every = vocab, eos, eos_every
+        self.calls: list = []
+
+    def forward(self, executions):
+        logits = torch.full((len(executions), self.vocab), -1.0)
+        for i, ex in enumerate(executions):
+            seq = ex.sequence
+            h = int(hashlib.sha256(f"{seq.request.request_id}:{seq.current_length}".encode())
+                    .hexdigest()[:8], 16)
+            tok = h % self.vocab
+            if self.eos is not None and self.eos_every and h % self.eos_every == 0:
+                tok = self.eos
+            logits[i, tok] = 1.0
+        self.calls.append(executions)
+        return logits
+
+
+def slot_checksum(slots) -> str:
+    return hashlib.sha256(np.asarray(slots, dtype=np.int64).tobytes()).hexdigest()[:16]
+
+
+@pytest.mark.parametrize("name", ["c1", "churn"])
+def test_engine_replays_reference_trace(name):
+    trace = json.loads((GOLDEN / f"engine_trace_{name}.json").read_text())
+    c = trace["config"]
+    cfg = eng.EngineConfiguration(block_size=c["block_size"], num_blocks=c["num_blocks"],
+                                  max_sequences=c["max_sequences"],
+                                  max_batched_tokens=c["max_batched_tokens"],
+                                  eos_token_id=c["eos_token_id"])
+    eos = 0 if trace["eos_every"] else None
+    runner = HashRunner(trace["vocab"], eos, trace["eos_every"])
+    engine = eng.Engine(configuration=cfg, model_runner=runner)
+    for r in trace["requests"]:
+        engine.submit(eng.Request(request_id=r["request_id"],
+                                  prompt_token_ids=tuple(r["prompt"]),
+                                  max_new_tokens=r["max_new_tokens"],
+                                  ignore_eos=r["ignore_eos"]))
+    for step_no, expected in enumerate(trace["steps"]):
+        assert engine.has_unfinished_requests
+        n = len(runner.calls)
+        engine.step()
+        got = []
+        if len(runner.calls) > n:
+            for ex in runner.calls[-1]:
+                slots = ex.slot_ids
+                got.append({
+                    "request_id": ex.sequence.request.request_id,
+                    "phase": ex.phase.value,
+                    "length": len(slots),
+                    "blocks": list(ex.block_ids),
+                    "last_slot": slots[-1],
+                    "slot_sha": slot_checksum(slots),
+                })
+        assert got == expected["executions"], f"step {step_no}"
+        assert engine.scheduler.num_preemptions == expected["preemptions"], f"step {step_no}"
+    assert not engine.has_unfinished_requests
+    finished = [{"request_id": s.request.request_id, "tokens": list(s.generated_token_ids),
+                 "finish_reason": s.finish_reason.value} for s in engine.finished_sequences]
+    assert finished == trace["finished"]
+    if name == "churn":
+        assert trace["num_preemptions"] > 0  # the trace does exercise recompute preemption
+
+
+def test_submit_rejections_match_reference_messages():
+    cfg = eng.EngineConfiguration(block_size=4, num_blocks=4, max_sequences=2,
+                                  max_batched_tokens=16)
+    s = eng.Scheduler(cfg)
+    with pytest.raises(ValueError, match="without chunked prefill"):
+        s.submit(eng.Request("a", tuple(range(17)), 1))
+    with pytest.raises(ValueError, match="re-prefilled without chunked prefill"):
+        s.submit(eng.Request("b", tuple(range(10)), 8))
+    cfg2 = eng.EngineConfiguration(block_size=4, num_blocks=2, max_sequences=2,
+                                   max_batched_tokens=64)
+    with pytest.raises(ValueError, match="more KV-cache blocks"):
+        eng.Scheduler(cfg2).submit(eng.Request("c", tuple(range(9)), 1))
+    s.submit(eng.Request("d", (1, 2), 2))
+    with pytest.raises(ValueError, match="already been submitted"):
+        s.submit(eng.Request("d", (1, 2), 2))
+
+
+def test_block_pool_fifo_order_and_errors():
+    pool = eng.BlockPool(4)
+    assert pool.allocate(2) == (0, 1)
+    pool.free(0)
+    assert pool.allocate(3) == (2, 3, 0)
+    with pytest.raises(RuntimeError, match="Not enough free blocks available"):
+        pool.allocate(1)
+    with pytest.raises(ValueError, match="Invalid block_id"):
+        pool.free(7)
+    table = eng.BlockTable(eng.BlockPool(8), block_size=4)
+    table.allocate_for_request("r", 5)
+    assert table.slot_for_position("r", 4) == 1 * 4 + 0
+    with pytest.raises(ValueError, match="No physical block exists"):
+        table.slot_for_position("r", 8)
+    with pytest.raises(ValueError, match="skips one or more logical blocks"):
+        table.append_token("r", 12)
