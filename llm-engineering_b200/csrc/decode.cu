@@ -27,7 +27,8 @@
 //    shared memory serves all G query heads of its group.
 //  * A sequence that lies inside one warp's range is finished from registers. A sequence
 //    cut by range boundaries leaves an fp32 partial (O, running max, running sum) per warp
-//    in the workspace; the last of those warps to finish (atomic counter) merges them.
+//    in the workspace; once a warp's stream is done it counts its partials in (atomic
+//    counter per sequence) and the last warp to report a sequence merges its partials.
 #include "common.cuh"
 
 namespace {
@@ -47,7 +48,8 @@ struct DecodeParams {
   int num_seqs;
   int group;       // G, query heads per KV head
   int layer;
-  int block_size;  // multiple of 16
+  int heads_per_unit;  // KV heads whose warps stream the same sub-block range in one CTA
+  int block_size;      // multiple of 16
   int64_t num_blocks;
   float scale_log2;  // softmax scale * log2(e)
   float* partials;   // [num_kv_heads][units][2][record]
@@ -57,10 +59,14 @@ struct DecodeParams {
 
 template <int D, int NT>
 struct Record {
-  // fp32 O^T in MMA fragment order ([D/16][NT][32 lanes][4]), then max and sum per query
-  // head, so that a warp writes and reads its partial with coalesced 16-byte accesses.
-  static constexpr int kO = (D / 16) * NT * 32 * 4;
-  static constexpr int kFloats = kO + 2 * NT * 8;
+  // Partial of one (unit, sequence): O^T / l in fp16, in MMA fragment order
+  // ([D/16][NT][32 lanes][4 halves] = one 8-byte access per lane), then the running max
+  // and sum per query head in fp32. Normalised values are bounded by max|v|, so fp16
+  // keeps ~3 decimal digits; the merge re-weights them with the exact fp32 sums.
+  static constexpr int kOBytes = (D / 16) * NT * 32 * 8;
+  static constexpr int kFloats = kOBytes / 4 + 2 * NT * 8;
+  static constexpr int kM = kOBytes / 4;       // float index of the maxima
+  static constexpr int kL = kOBytes / 4 + NT * 8;  // float index of the sums
 };
 
 struct Range {
@@ -236,13 +242,18 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
                                              ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int head = blockIdx.y;  // KV head
+  // Warps w and w+1 (2 KV heads) or w..w+3 (4 heads) stream the same sub-blocks for
+  // different heads, so both halves of every 512-byte slot row are fetched by one SM at
+  // nearly the same time (one DRAM page opening instead of two).
+  const int hpu = p.heads_per_unit;
+  const int head = blockIdx.y * hpu + warp % hpu;  // KV head
   uint8_t* ring = smem + (size_t)warp * S * kStageBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)W * S * kStageBytes) + warp * S;
 
   Range r;
-  const int64_t unit = (int64_t)blockIdx.x * W + warp;
-  find_range(p, (int64_t)gridDim.x * W, unit, r);
+  const int64_t units_per_cta = W / hpu;
+  const int64_t unit = (int64_t)blockIdx.x * units_per_cta + warp / hpu;
+  find_range(p, (int64_t)gridDim.x * units_per_cta, unit, r);
   if (r.begin >= r.end) return;
   const int64_t n = r.end - r.begin;
   const int64_t parts = r.parts;
@@ -259,7 +270,7 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
   SlotResolver res{r.seq0, r.cb0, r.begin, n};
   int64_t buf_base = 0;  // items [buf_base, buf_base + 32) are in slot_lo
   int64_t slot_lo = res(p, 0, lane, num_slots);
-  int64_t slot_hi = n > 32 ? res(p, 32, lane, num_slots) : -1;
+  int64_t slot_hi = -1;  // resolved right after the first copies are out
   int64_t issued = 0;
   bool aborted = false;
 
@@ -282,6 +293,7 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
     issued = k + 1;
   };
   for (int64_t k = 0; k < S && k < n; ++k) issue(k);
+  if (n > 32) slot_hi = res(p, 32, lane, num_slots);
 
   const int g8 = lane >> 2;  // row group (0..7)
   const int t4 = lane & 3;   // thread in group (0..3)
@@ -289,6 +301,30 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
   int64_t cb = r.cb0;
   int64_t gidx = r.begin;
   int64_t k = 0;  // local item index
+
+  // Normalised output rows of one sequence from O^T fragments and per-head sums.
+  auto write_out = [&](int sq, float (&o)[D / 16][NT][4], float (&lsum)[NT][2]) {
+#pragma unroll
+    for (int nn = 0; nn < NT; ++nn) {
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const int qh = nn * 8 + 2 * t4 + cc;
+        if (qh >= p.group) continue;
+        const float inv = lsum[nn][cc] > 0.f ? 1.f / lsum[nn][cc] : 0.f;
+        T* orow = reinterpret_cast<T*>(p.out) + (int64_t)sq * p.o_tok +
+                  (int64_t)(head * p.group + qh) * p.o_head;
+#pragma unroll
+        for (int i = 0; i < D / 16; ++i) {
+          orow[i * 16 + g8] = from_f32<T>(o[i][nn][cc] * inv);
+          orow[i * 16 + g8 + 8] = from_f32<T>(o[i][nn][2 + cc] * inv);
+        }
+      }
+    }
+  };
+  int npend = 0;  // sequences this warp left a partial for (at most its first and last)
+  int pend_seq[2] = {0, 0};
+  int64_t pend_cb[2] = {0, 0};
+  int pend_nb[2] = {0, 0};
 
   while (gidx < r.end) {
     const int ctx = __ldg(p.context_lens + seq);
@@ -308,6 +344,15 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
     const int lb0 = (int)(gidx - cb);
     const int64_t seg_end = min(r.end, cb + nb);
     const int lb1 = (int)(seg_end - cb);
+
+    // Warm L1 with the next sequence's query rows (read when its segment starts).
+    if (seg_end < r.end && lb1 == nb && seq + 1 < p.num_seqs) {
+      const T* nq = reinterpret_cast<const T*>(p.q) + (int64_t)(seq + 1) * p.q_tok +
+                    (int64_t)head * p.group * p.q_head;
+      const int lines = (p.group * D * (int)sizeof(T) + 127) / 128;
+      if (lane < lines && p.q_head == D)
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const uint8_t*>(nq) + lane * 128));
+    }
 
     // Q fragments (B operand of S^T = K Q^T): Q[qh = g8 + 8n][16kk + 2t4 (+8)].
     uint32_t qf[NT][D / 16][2];
@@ -454,101 +499,42 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
       }
     }
     const bool complete = (lb0 == 0) && (lb1 == nb);
-    auto write_out = [&](float (&o)[D / 16][NT][4], float (&lsum)[NT][2]) {
-#pragma unroll
-      for (int nn = 0; nn < NT; ++nn) {
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          const int qh = nn * 8 + 2 * t4 + cc;
-          if (qh >= p.group) continue;
-          const float inv = lsum[nn][cc] > 0.f ? 1.f / lsum[nn][cc] : 0.f;
-          T* orow = reinterpret_cast<T*>(p.out) + (int64_t)seq * p.o_tok +
-                    (int64_t)(head * p.group + qh) * p.o_head;
-#pragma unroll
-          for (int i = 0; i < D / 16; ++i) {
-            orow[i * 16 + g8] = from_f32<T>(o[i][nn][cc] * inv);
-            orow[i * 16 + g8 + 8] = from_f32<T>(o[i][nn][2 + cc] * inv);
-          }
-        }
-      }
-    };
     if (complete) {
-      write_out(acc, l_run);
+      write_out(seq, acc, l_run);
     } else {
       const int slot_idx = (cb + lb0 == r.begin) ? 0 : 1;  // first segment of this unit or not
       float* rec = p.partials + (((size_t)head * parts + unit) * 2 + slot_idx) * Rec::kFloats;
 #pragma unroll
-      for (int i = 0; i < D / 16; ++i)
+      for (int nn = 0; nn < NT; ++nn) {
+        const float i0 = l_run[nn][0] > 0.f ? 1.f / l_run[nn][0] : 0.f;
+        const float i1 = l_run[nn][1] > 0.f ? 1.f / l_run[nn][1] : 0.f;
 #pragma unroll
-        for (int nn = 0; nn < NT; ++nn)
-          reinterpret_cast<float4*>(rec)[(i * NT + nn) * 32 + lane] =
-              make_float4(acc[i][nn][0], acc[i][nn][1], acc[i][nn][2], acc[i][nn][3]);
+        for (int i = 0; i < D / 16; ++i) {
+          __half2 lo = __floats2half2_rn(acc[i][nn][0] * i0, acc[i][nn][1] * i1);
+          __half2 hi = __floats2half2_rn(acc[i][nn][2] * i0, acc[i][nn][3] * i1);
+          uint2 v;
+          v.x = *reinterpret_cast<uint32_t*>(&lo);
+          v.y = *reinterpret_cast<uint32_t*>(&hi);
+          reinterpret_cast<uint2*>(rec)[(i * NT + nn) * 32 + lane] = v;
+        }
+      }
       if (g8 == 0) {
 #pragma unroll
         for (int nn = 0; nn < NT; ++nn) {
-          rec[Rec::kO + nn * 8 + 2 * t4] = m_run[nn][0];
-          rec[Rec::kO + nn * 8 + 2 * t4 + 1] = m_run[nn][1];
-          rec[Rec::kO + NT * 8 + nn * 8 + 2 * t4] = l_run[nn][0];
-          rec[Rec::kO + NT * 8 + nn * 8 + 2 * t4 + 1] = l_run[nn][1];
+          rec[Rec::kM + nn * 8 + 2 * t4] = m_run[nn][0];
+          rec[Rec::kM + nn * 8 + 2 * t4 + 1] = m_run[nn][1];
+          rec[Rec::kL + nn * 8 + 2 * t4] = l_run[nn][0];
+          rec[Rec::kL + nn * 8 + 2 * t4 + 1] = l_run[nn][1];
         }
       }
-      const int64_t u_first = owner_unit(cb, r.total, parts);
-      const int64_t u_last = owner_unit(cb + nb - 1, r.total, parts);
-      __syncwarp();
-      int last = 0;
-      if (lane == 0) {
-        __threadfence();  // this warp's partial is visible before the count says so
-        int32_t* ctr = p.counters + (size_t)head * p.num_seqs + seq;
-        const int prev = atomicAdd(ctr, 1);
-        last = prev == (int)(u_last - u_first);
-        if (last) {
-          *ctr = 0;  // leave the workspace zeroed for the next launch
-          __threadfence();
-        }
-      }
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (last) {
-        // Merge every unit's partial of this sequence (this warp's own included), reading
-        // through L2: the other partials were written by other SMs.
-        float M[NT][2];
-#pragma unroll
-        for (int nn = 0; nn < NT; ++nn) M[nn][0] = M[nn][1] = -INFINITY;
-        for (int64_t u = u_first; u <= u_last; ++u) {
-          const int si = (u == u_first && range_start(u, r.total, parts) != cb) ? 1 : 0;
-          const float* pr = p.partials + (((size_t)head * parts + u) * 2 + si) * Rec::kFloats;
-#pragma unroll
-          for (int nn = 0; nn < NT; ++nn) {
-            M[nn][0] = fmaxf(M[nn][0], __ldcg(pr + Rec::kO + nn * 8 + 2 * t4));
-            M[nn][1] = fmaxf(M[nn][1], __ldcg(pr + Rec::kO + nn * 8 + 2 * t4 + 1));
-          }
-        }
-        float L[NT][2];
-#pragma unroll
-        for (int nn = 0; nn < NT; ++nn) {
-          L[nn][0] = L[nn][1] = 0.f;
-#pragma unroll
-          for (int i = 0; i < D / 16; ++i) acc[i][nn][0] = acc[i][nn][1] = acc[i][nn][2] = acc[i][nn][3] = 0.f;
-        }
-        for (int64_t u = u_first; u <= u_last; ++u) {
-          const int si = (u == u_first && range_start(u, r.total, parts) != cb) ? 1 : 0;
-          const float* pr = p.partials + (((size_t)head * parts + u) * 2 + si) * Rec::kFloats;
-#pragma unroll
-          for (int nn = 0; nn < NT; ++nn) {
-            const float sc0 = fast_exp2(__ldcg(pr + Rec::kO + nn * 8 + 2 * t4) - M[nn][0]);
-            const float sc1 = fast_exp2(__ldcg(pr + Rec::kO + nn * 8 + 2 * t4 + 1) - M[nn][1]);
-            L[nn][0] += __ldcg(pr + Rec::kO + NT * 8 + nn * 8 + 2 * t4) * sc0;
-            L[nn][1] += __ldcg(pr + Rec::kO + NT * 8 + nn * 8 + 2 * t4 + 1) * sc1;
-#pragma unroll
-            for (int i = 0; i < D / 16; ++i) {
-              const float4 v = __ldcg(reinterpret_cast<const float4*>(pr) + (i * NT + nn) * 32 + lane);
-              acc[i][nn][0] += v.x * sc0;
-              acc[i][nn][1] += v.y * sc1;
-              acc[i][nn][2] += v.z * sc0;
-              acc[i][nn][3] += v.w * sc1;
-            }
-          }
-        }
-        write_out(acc, L);
+      // The counter update (which needs a fence) and the possible merge wait until this
+      // warp's stream is finished: a fence issued mid-stream stalls behind the warp's
+      // outstanding loads and leaves its stages unrefilled.
+      if (npend < 2) {
+        pend_seq[npend] = seq;
+        pend_cb[npend] = cb;
+        pend_nb[npend] = nb;
+        ++npend;
       }
     }
     gidx = seg_end;
@@ -562,6 +548,95 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
   if (lane == 0) {
     for (int64_t kk = k; kk < issued; ++kk)
       mbar_wait_bounded(&full[kk % S], (uint32_t)((kk / S) & 1), nullptr);
+  }
+
+  // Count this warp's partials in; the last unit to report a sequence merges all of its
+  // partials (its own included), reading through L2 since other SMs wrote them.
+  if (npend == 0) return;
+  __syncwarp();
+  int last_mask = 0;
+  if (lane == 0) {
+    __threadfence();  // the partials are visible before the counts say so
+    int prev[2] = {0, 0};
+    for (int j = 0; j < npend; ++j)  // both atomics in flight together
+      prev[j] = atomicAdd(p.counters + (size_t)head * p.num_seqs + pend_seq[j], 1);
+    for (int j = 0; j < npend; ++j) {
+      const int64_t uf = owner_unit(pend_cb[j], r.total, parts);
+      const int64_t ul = owner_unit(pend_cb[j] + pend_nb[j] - 1, r.total, parts);
+      if (prev[j] == (int)(ul - uf)) {
+        p.counters[(size_t)head * p.num_seqs + pend_seq[j]] = 0;  // zeroed for the next launch
+        last_mask |= 1 << j;
+      }
+    }
+    if (last_mask) __threadfence();
+  }
+  last_mask = __shfl_sync(0xffffffffu, last_mask, 0);
+  for (int j = 0; j < npend; ++j) {
+    if (!((last_mask >> j) & 1)) continue;
+    const int sq = pend_seq[j];
+    const int64_t scb = pend_cb[j];
+    const int64_t u_first = owner_unit(scb, r.total, parts);
+    const int64_t u_last = owner_unit(scb + pend_nb[j] - 1, r.total, parts);
+    float M[NT][2], L[NT][2];
+    float O[D / 16][NT][4];
+#pragma unroll
+    for (int nn = 0; nn < NT; ++nn) {
+      M[nn][0] = M[nn][1] = -INFINITY;
+      L[nn][0] = L[nn][1] = 0.f;
+#pragma unroll
+      for (int i = 0; i < D / 16; ++i) O[i][nn][0] = O[i][nn][1] = O[i][nn][2] = O[i][nn][3] = 0.f;
+    }
+    // One online pass; four contributors' loads are issued before any of them is used.
+    constexpr int kBatch = 4;
+    for (int64_t u0 = u_first; u0 <= u_last; u0 += kBatch) {
+      float mv[kBatch][NT][2], lv[kBatch][NT][2];
+      uint2 ov[kBatch][D / 16][NT];
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int64_t u = u0 + b;
+        const bool have = u <= u_last;
+        const int si = (u == u_first && range_start(u, r.total, parts) != scb) ? 1 : 0;
+        const float* pr =
+            p.partials + (((size_t)head * parts + (have ? u : u_first)) * 2 + si) * Rec::kFloats;
+#pragma unroll
+        for (int nn = 0; nn < NT; ++nn) {
+          mv[b][nn][0] = have ? __ldcg(pr + Rec::kM + nn * 8 + 2 * t4) : -INFINITY;
+          mv[b][nn][1] = have ? __ldcg(pr + Rec::kM + nn * 8 + 2 * t4 + 1) : -INFINITY;
+          lv[b][nn][0] = have ? __ldcg(pr + Rec::kL + nn * 8 + 2 * t4) : 0.f;
+          lv[b][nn][1] = have ? __ldcg(pr + Rec::kL + nn * 8 + 2 * t4 + 1) : 0.f;
+#pragma unroll
+          for (int i = 0; i < D / 16; ++i)
+            ov[b][i][nn] = have ? __ldcg(reinterpret_cast<const uint2*>(pr) + (i * NT + nn) * 32 + lane)
+                                : make_uint2(0u, 0u);
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+#pragma unroll
+        for (int nn = 0; nn < NT; ++nn) {
+          float w[2], a[2];
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            const float mn = fmaxf(M[nn][cc], mv[b][nn][cc]);
+            a[cc] = mn == -INFINITY ? 0.f : fast_exp2(M[nn][cc] - mn);  // rescale old
+            w[cc] = mn == -INFINITY ? 0.f : fast_exp2(mv[b][nn][cc] - mn) * lv[b][nn][cc];
+            L[nn][cc] = L[nn][cc] * a[cc] + w[cc];
+            M[nn][cc] = mn;
+          }
+#pragma unroll
+          for (int i = 0; i < D / 16; ++i) {
+            const uint2 v = ov[b][i][nn];
+            const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+            const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+            O[i][nn][0] = O[i][nn][0] * a[0] + lo.x * w[0];
+            O[i][nn][1] = O[i][nn][1] * a[1] + lo.y * w[1];
+            O[i][nn][2] = O[i][nn][2] * a[0] + hi.x * w[0];
+            O[i][nn][3] = O[i][nn][3] * a[1] + hi.y * w[1];
+          }
+        }
+      }
+    }
+    write_out(sq, O, L);
   }
 }
 
@@ -648,10 +723,21 @@ int prepare(Plan& pl) {
   return B2P_OK;
 }
 
-// CTAs per KV head: one wave over all SMs.
-int64_t ctas_per_head(int ctas_per_sm, int num_kv_heads) {
+// KV heads that share one sub-block range inside a CTA (a divisor of the head count that
+// fits the CTA's warps).
+int heads_per_unit(int num_kv_heads, int warps) {
+  // Measured on B200: pairing the warps of both KV heads on one range (both halves of each
+  // slot row fetched by one SM) was slower than one head per CTA (121 vs 113 us on the
+  // 256-sequence, 12/2-head benchmark), so every warp streams its own range.
+  (void)num_kv_heads;
+  (void)warps;
+  return 1;
+}
+
+// CTAs along x (one wave over all SMs for the grid.y head groups).
+int64_t ctas_x(int ctas_per_sm, int num_kv_heads, int hpu) {
   const int64_t slots = (int64_t)b2p_host::sm_count() * ctas_per_sm;
-  const int64_t c = slots / num_kv_heads;
+  const int64_t c = slots / (num_kv_heads / hpu);
   return c < 1 ? 1 : c;
 }
 
@@ -673,7 +759,8 @@ extern "C" size_t b2p_paged_decode_workspace_size(int num_seqs, int num_q_heads,
   Plan pl;
   if (!select_plan(B2P_BF16, head_dim, group, pl)) return 16;  // CUDA-core path: none needed
   // Upper bound over occupancies (at most 8 CTAs per SM are used).
-  const int64_t units = ctas_per_head(8, num_kv_heads) * pl.warps;
+  const int hpu = heads_per_unit(num_kv_heads, pl.warps);
+  const int64_t units = ctas_x(8, num_kv_heads, hpu) * (pl.warps / hpu);
   return workspace_bytes(num_seqs, num_kv_heads, units, pl.record);
 }
 
@@ -721,8 +808,10 @@ extern "C" int b2p_paged_decode(const void* q, int64_t q_tok_stride, int64_t q_h
   if (!workspace) return B2P_EWORKSPACE;
   int rc = prepare(pl);
   if (rc != B2P_OK) return rc;
-  const int64_t ctas = ctas_per_head(pl.ctas_per_sm, num_kv_heads);
-  const size_t need = workspace_bytes(num_seqs, num_kv_heads, ctas * pl.warps, pl.record);
+  const int hpu = heads_per_unit(num_kv_heads, pl.warps);
+  const int64_t ctas = ctas_x(pl.ctas_per_sm, num_kv_heads, hpu);
+  const size_t need =
+      workspace_bytes(num_seqs, num_kv_heads, ctas * (pl.warps / hpu), pl.record);
   if (workspace_size < need) return B2P_EWORKSPACE;
 
   CUtensorMap kmap, vmap;
@@ -746,6 +835,7 @@ extern "C" int b2p_paged_decode(const void* q, int64_t q_tok_stride, int64_t q_h
   p.num_seqs = num_seqs;
   p.group = group;
   p.layer = (int)layer_index;
+  p.heads_per_unit = hpu;
   p.block_size = block_size;
   p.num_blocks = num_slots / block_size;
   p.scale_log2 = scale * kLog2e;
@@ -754,7 +844,7 @@ extern "C" int b2p_paged_decode(const void* q, int64_t q_tok_stride, int64_t q_h
                                         counters_bytes(num_seqs, num_kv_heads));
   p.err = err_flag;
 
-  dim3 grid((unsigned)ctas, (unsigned)num_kv_heads);
+  dim3 grid((unsigned)ctas, (unsigned)(num_kv_heads / hpu));
   void* args[] = {&kmap, &vmap, &p};
   cudaError_t e = cudaLaunchKernel(pl.fn, grid, dim3(pl.warps * 32), args, (size_t)pl.smem,
                                    static_cast<cudaStream_t>(stream));
