@@ -129,8 +129,11 @@ B2P_API int b2p_paged_decode(const void* q, int64_t q_tok_stride, int64_t q_head
  * position context_lens[i] - q_len_i + j and attends keys 0..that position. When
  * q_len_i == context_lens[i] this is the reference's whole-history prefill.
  *   q   : [total_q, num_q_heads, head_dim]    out : same shape
- *   total_q = cu_seqlens_q[num_seqs] and max_q_len = the longest query run, both known
- *   to the host that built cu_seqlens_q (they size the grid; no device read-back).
+ *   cu_seqlens_q holds absolute row offsets into q and need not start at 0, so a caller
+ *   can run the trailing executions of a packed batch by passing views of its metadata.
+ *   total_q = cu_seqlens_q[num_seqs] - cu_seqlens_q[0] and max_q_len = the longest query
+ *   run, both known to the host that built cu_seqlens_q (they size the grid; no device
+ *   read-back).
  * bf16/f16 with head_dim 128 and block_size % 16 == 0 run on tcgen05 tensor cores
  * (TMEM accumulators); other shapes and fp32 run on CUDA cores.
  */

@@ -41,7 +41,9 @@ template <typename T>
 __global__ void __launch_bounds__(kWarps * 32) paged_attn_simt(const SimtParams p) {
   __shared__ float qs[kWarps][kMaxD];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t row = blockIdx.x;
+  // Decode mode: row i is sequence i. Prefill mode: rows start at cu_q[0], which lets a
+  // caller run a trailing slice of a packed batch with views of the metadata.
+  const int64_t row = blockIdx.x + (p.cu_q == nullptr ? 0 : __ldg(p.cu_q));
   const int qh = blockIdx.y * kWarps + warp;
   if (qh >= p.num_q_heads) return;
 

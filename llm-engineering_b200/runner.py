@@ -1,0 +1,326 @@
+"""B200 paged model runner — the drop-in for the reference's ``PagedModelRunner``.
+
+Reference path replaced (serving/engine/paged_model_runner.py:44-91): one packed HF
+forward per engine step, with ``HFBatchedPagedCache`` (serving/engine/
+hf_batched_paged_cache.py:52-148) scattering new K/V, gathering every history and
+concatenating it, a dense additive block-diagonal mask (serving/engine/attention_mask.py),
+and HF SDPA over all packed keys.
+
+Here the same ``ModelRunner.forward(executions) -> (B, vocab)`` interface
+(serving/engine/model_runner.py:11-26) drives:
+  * K4 (``ops.build_metadata``): cu_seqlens, positions, write slots and logit rows built on
+    the GPU from a per-step descriptor (query length, key length, table row per execution)
+    and the step's block tables;
+  * ``B200PagedCache.update`` (the HF ``Cache`` hook, transformers/models/qwen2/
+    modeling_qwen2.py:225): K1 writes the step's K/V rows into the pool and returns
+    without gathering anything;
+  * ``paged_attention`` (registered with HF's ``AttentionInterface`` under
+    ``ATTENTION_NAME``; the model calls it at modeling_qwen2.py:227-240): K2 for the
+    leading decode executions and K3 for the prefill / chunked-prefill ones, reading the
+    pool in place through block tables. A registered name outside HF's mask registry also
+    makes HF skip building any mask.
+  * ``logits_to_keep`` restricts the LM head to each execution's last query row, which is
+    exactly the rows the reference keeps with ``index_select`` (paged_model_runner.py:85-91).
+
+Executions may come from the reference engine (``slot_ids`` over the whole history) or
+from this package's engine (``block_ids``). Slot ids that follow the block structure
+(``slot = block * block_size + pos % block_size``, which is what the reference's
+``BlockTable`` produces) become block tables; any other slot list is run as a table of
+one-slot blocks, which the CUDA-core attention kernel accepts.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import contextvars
+from collections.abc import Sequence
+from dataclasses import dataclass
+from typing import Any
+
+import numpy as np
+import torch
+from transformers.cache_utils import Cache
+
+from . import ops as _ops
+
+ATTENTION_NAME = "b200_paged"
+PREFILL, DECODE = "prefill", "decode"
+
+_active_batch: contextvars.ContextVar[StepBatch | None] = contextvars.ContextVar(
+    "b200_paged_step", default=None)
+
+
+@dataclass
+class StepBatch:
+    """Device metadata of one packed forward."""
+
+    kernels: Any
+    key_cache: torch.Tensor
+    value_cache: torch.Tensor
+    block_size: int
+    total_q: int
+    num_execs: int
+    num_decode: int       # leading executions that are single-token decodes
+    max_q_len: int
+    slot_mapping: torch.Tensor   # int32 [total_q]
+    positions: torch.Tensor      # int64 [total_q]
+    cu_seqlens_q: torch.Tensor   # int32 [B + 1]
+    context_lens: torch.Tensor   # int32 [B]
+    block_tables: torch.Tensor   # int32 [B, W]
+    logit_indices: torch.Tensor  # int64 [B]
+    workspace: torch.Tensor
+    err: torch.Tensor
+
+
+def _phase_of(execution) -> str:
+    phase = getattr(execution.phase, "value", execution.phase)
+    if phase not in (PREFILL, DECODE):
+        raise ValueError(f"Unsupported execution phase: {execution.phase}")
+    return phase
+
+
+def paged_attention(module: torch.nn.Module, query: torch.Tensor, key: torch.Tensor,
+                    value: torch.Tensor, attention_mask: torch.Tensor | None,
+                    dropout: float = 0.0, scaling: float | None = None, **kwargs: Any):
+    """HF attention-interface function: paged attention of the packed query rows.
+
+    query: (1, HQ, Tq, D) after RoPE. ``key``/``value`` are this step's new rows (already
+    written to the pool by ``B200PagedCache.update``); the kernels read every history
+    from the pool. Returns (attn_output (1, Tq, HQ, D), None) like HF's SDPA path.
+    """
+    del key, value, attention_mask, kwargs
+    batch = _active_batch.get()
+    if batch is None:
+        raise RuntimeError(f"{ATTENTION_NAME} attention used outside B200PagedModelRunner.forward")
+    if dropout:
+        raise ValueError("paged attention does not implement dropout")
+    layer = module.layer_idx
+    q = query[0].transpose(0, 1)  # (Tq, HQ, D) view, head_dim contiguous
+    if scaling is None:
+        scaling = q.shape[-1] ** -0.5
+    k = batch.kernels
+    out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    nd = batch.num_decode
+    if nd:
+        k.paged_decode(q[:nd], batch.key_cache, batch.value_cache, layer, batch.block_tables[:nd],
+                       batch.context_lens[:nd], batch.block_size, scaling, out=out[:nd],
+                       workspace=batch.workspace, err_flag=batch.err)
+    if nd < batch.num_execs:
+        k.paged_prefill(q, batch.key_cache, batch.value_cache, layer, batch.block_tables[nd:],
+                        batch.cu_seqlens_q[nd:], batch.context_lens[nd:], batch.max_q_len,
+                        batch.block_size, scaling, out=out, err_flag=batch.err,
+                        num_rows=batch.total_q - nd)
+    return out.unsqueeze(0), None
+
+
+def _register_attention() -> None:
+    from transformers import AttentionInterface
+
+    AttentionInterface.register(ATTENTION_NAME, paged_attention)
+
+
+class B200PagedCache(Cache):
+    """HF cache hook: writes each layer's new K/V rows into the pool (K1) and returns the
+    states unchanged — there is no gathered history to hand back."""
+
+    def __init__(self, batch: StepBatch) -> None:
+        super().__init__(layers=[])
+        self._batch = batch
+
+    def update(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int,
+               *args: Any, **kwargs: Any) -> tuple[torch.Tensor, torch.Tensor]:
+        del args, kwargs
+        if key_states.ndim != 4:
+            raise ValueError("key_states must have shape (batch, kv_heads, tokens, head_dim).")
+        if value_states.ndim != 4:
+            raise ValueError("value_states must have shape (batch, kv_heads, tokens, head_dim).")
+        if key_states.shape != value_states.shape:
+            raise ValueError("key_states and value_states must have matching shapes.")
+        if key_states.shape[0] != 1:
+            raise ValueError("Packed execution must use one Hugging Face batch row.")
+        if key_states.shape[2] != self._batch.total_q:
+            raise ValueError(
+                "Packed KV query length does not match BatchLayout: "
+                f"expected {self._batch.total_q}, got {key_states.shape[2]}.")
+        b = self._batch
+        b.kernels.kv_write(b.key_cache, b.value_cache, layer_idx, b.slot_mapping,
+                           key_states[0].transpose(0, 1), value_states[0].transpose(0, 1),
+                           b.err)
+        return key_states, value_states
+
+    def get_seq_length(self, layer_idx: int = 0) -> int:
+        raise RuntimeError(
+            "B200PagedCache does not expose one scalar sequence length for packed execution "
+            f"(layer {layer_idx}).")
+
+    def get_query_offset(self, layer_idx: int = 0) -> int:
+        raise RuntimeError(
+            "B200PagedCache does not expose one scalar query offset for packed execution "
+            f"(layer {layer_idx}).")
+
+    def get_mask_sizes(self, query_length: int, layer_idx: int) -> tuple[int, int]:
+        raise RuntimeError(
+            "B200PagedCache builds no attention mask; cache-derived mask sizing is unsupported "
+            f"(query_length={query_length}, layer={layer_idx}).")
+
+
+def _storage_of(paged_cache) -> Any:
+    return getattr(paged_cache, "storage", paged_cache)
+
+
+class B200PagedModelRunner:
+    """``ModelRunner`` implementation running the packed forward on the paged kernels.
+
+    Args:
+        model: a Hugging Face causal LM whose attention goes through ``AttentionInterface``
+            (Qwen2 and the other functional-attention models).
+        device: CUDA device of the model and the pool.
+        paged_cache: the reference's ``PagedKVCache`` (or anything with ``.storage``) or a
+            storage object exposing ``key_cache``, ``value_cache`` and ``block_size``
+            (the reference's ``PagedKVStorage`` or ``llm_engineering_b200.storage``).
+        kernels: the kernel module (tests substitute a CPU implementation).
+    """
+
+    def __init__(self, model, device: torch.device, paged_cache, *, kernels: Any = None) -> None:
+        self._model = model
+        self._device = torch.device(device)
+        self._storage = _storage_of(paged_cache)
+        self._kernels = kernels if kernels is not None else _ops
+        _register_attention()
+        model.set_attn_implementation(ATTENTION_NAME)
+        model.eval()
+        cfg = model.config
+        self._hq = cfg.num_attention_heads
+        self._hkv = cfg.num_key_value_heads
+        self._head_dim = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
+        self._workspace = torch.zeros(16, dtype=torch.uint8, device=self._device)
+        self._err = torch.zeros(1, dtype=torch.int32, device=self._device)
+
+    # ------------------------------------------------------------------ host metadata
+    @staticmethod
+    def _token_ids(seq, start: int, stop: int) -> np.ndarray:
+        """Token ids of positions [start, stop) without building the whole history."""
+        prompt = seq.request.prompt_token_ids
+        n = len(prompt)
+        if stop <= n:
+            return np.asarray(prompt[start:stop], dtype=np.int64)
+        gen = seq.generated_token_ids
+        if start >= n:
+            return np.asarray(gen[start - n:stop - n], dtype=np.int64)
+        return np.concatenate([np.asarray(prompt[start:], dtype=np.int64),
+                               np.asarray(gen[:stop - n], dtype=np.int64)])
+
+    def _describe(self, executions: Sequence) -> dict:
+        bs = self._storage.block_size
+        phases, qlens, lengths, tables, is_slots, token_parts = [], [], [], [], [], []
+        for ex in executions:
+            phase = _phase_of(ex)
+            length = getattr(ex, "length", None) or ex.sequence.current_length
+            qlen = getattr(ex, "query_length", None)
+            if qlen is None:  # reference ModelExecution: BatchLayout semantics
+                qlen = length if phase == PREFILL else 1
+            blocks = getattr(ex, "block_ids", None)
+            slot_list = False
+            if blocks is None:
+                slots = np.asarray(ex.slot_ids, dtype=np.int64)
+                if len(slots) != length:
+                    raise ValueError("slot_ids length must equal the sequence current length.")
+                cand = slots[::bs] // bs
+                pos = np.arange(length, dtype=np.int64)
+                if np.array_equal(cand[pos // bs] * bs + pos % bs, slots):
+                    blocks = cand
+                else:  # not block-structured: keep the per-position slots
+                    blocks, slot_list = slots, True
+            tables.append(np.asarray(blocks, dtype=np.int64))
+            is_slots.append(slot_list)
+            token_parts.append(self._token_ids(ex.sequence, length - qlen, length))
+            phases.append(phase)
+            qlens.append(qlen)
+            lengths.append(length)
+        if any(is_slots):  # express every table as one-slot blocks (block size 1)
+            expanded = []
+            for t, n, sl in zip(tables, lengths, is_slots, strict=True):
+                if sl:
+                    expanded.append(t)
+                else:
+                    pos = np.arange(n, dtype=np.int64)
+                    expanded.append(t[pos // bs] * bs + pos % bs)
+            tables, bs = expanded, 1
+        return {"phases": phases, "qlens": qlens, "lengths": lengths, "tables": tables,
+                "tokens": np.concatenate(token_parts), "block_size": bs}
+
+    def _build_batch(self, executions: Sequence) -> tuple[StepBatch, torch.Tensor]:
+        d = self._describe(executions)
+        n = len(executions)
+        dev = self._device
+        num_decode = 0
+        while num_decode < n and d["phases"][num_decode] == DECODE:
+            num_decode += 1
+        width = max(1, max(len(t) for t in d["tables"]))
+        host = np.full((3 * n + n * width,), -1, dtype=np.int32)
+        host[0:n] = d["qlens"]
+        host[n:2 * n] = d["lengths"]
+        host[2 * n:3 * n] = np.arange(n, dtype=np.int32)
+        tab = host[3 * n:].reshape(n, width)
+        for i, t in enumerate(d["tables"]):
+            tab[i, :len(t)] = t
+        staged = torch.from_numpy(host)
+        tokens = torch.from_numpy(d["tokens"])
+        if dev.type == "cuda":
+            staged = staged.pin_memory()
+            tokens = tokens.pin_memory()
+        dev_i32 = staged.to(dev, non_blocking=True)
+        input_ids = tokens.to(dev, non_blocking=True)
+        qlens = dev_i32[0:n]
+        ctx = dev_i32[n:2 * n]
+        rows = dev_i32[2 * n:3 * n]
+        tables = dev_i32[3 * n:].view(n, width)
+        total_q = int(sum(d["qlens"]))
+        md = self._kernels.build_metadata(qlens, ctx, rows, tables, d["block_size"], total_q, 0,
+                                          self._err)
+        need = self._kernels.decode_workspace_size(max(num_decode, 1), self._hq, self._hkv,
+                                                   self._head_dim)
+        if self._workspace.numel() < need:
+            self._workspace = torch.zeros(need, dtype=torch.uint8, device=dev)
+        batch = StepBatch(
+            kernels=self._kernels, key_cache=self._storage.key_cache,
+            value_cache=self._storage.value_cache, block_size=d["block_size"], total_q=total_q,
+            num_execs=n, num_decode=num_decode, max_q_len=max(d["qlens"]),
+            slot_mapping=md["slot_mapping"], positions=md["positions"],
+            cu_seqlens_q=md["cu_seqlens_q"], context_lens=ctx, block_tables=tables,
+            logit_indices=md["logit_indices"], workspace=self._workspace, err=self._err)
+        return batch, input_ids
+
+    # ------------------------------------------------------------------ ModelRunner
+    def forward(self, executions: Sequence) -> torch.Tensor:
+        """Next-token logits (B, vocab) for the executions, in their order."""
+        if not executions:
+            raise ValueError("At least one execution is required.")
+        batch, input_ids = self._build_batch(executions)
+        cache = B200PagedCache(batch)
+        token = _active_batch.set(batch)
+        try:
+            with torch.inference_mode():
+                out = self._model(input_ids=input_ids.unsqueeze(0),
+                                  position_ids=batch.positions.unsqueeze(0), attention_mask=None,
+                                  past_key_values=cache, use_cache=True,
+                                  logits_to_keep=batch.logit_indices)
+        finally:
+            _active_batch.reset(token)
+        return out.logits[0]
+
+    def device_error(self) -> int:
+        """Bits the kernels reported since the last call (0 = none); clears them."""
+        v = int(self._err.item())
+        self._err.zero_()
+        return v
+
+
+@contextlib.contextmanager
+def active(batch: StepBatch):
+    """Make ``batch`` the current step for ``paged_attention`` (used by tests)."""
+    token = _active_batch.set(batch)
+    try:
+        yield
+    finally:
+        _active_batch.reset(token)
