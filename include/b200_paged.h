@@ -131,9 +131,9 @@ B2P_API int b2p_paged_decode(const void* q, int64_t q_tok_stride, int64_t q_head
  *   q   : [total_q, num_q_heads, head_dim]    out : same shape
  *   cu_seqlens_q holds absolute row offsets into q and need not start at 0, so a caller
  *   can run the trailing executions of a packed batch by passing views of its metadata.
- *   total_q = cu_seqlens_q[num_seqs] - cu_seqlens_q[0] and max_q_len = the longest query
- *   run, both known to the host that built cu_seqlens_q (they size the grid; no device
- *   read-back).
+ *   total_q = the number of rows of q and out (>= cu_seqlens_q[num_seqs]); it bounds the
+ *   grid and the TMA view of q, so no device value is read back on the host.
+ *   max_q_len = the longest query run (informational).
  * bf16/f16 with head_dim 128 and block_size % 16 == 0 run on tcgen05 tensor cores
  * (TMEM accumulators); other shapes and fp32 run on CUDA cores.
  */

@@ -60,6 +60,7 @@ __global__ void __launch_bounds__(kWarps * 32) paged_attn_simt(const SimtParams 
       if (__ldg(p.cu_q + mid) <= row) lo = mid; else hi = mid - 1;
     }
     seq = lo;
+    if (row >= __ldg(p.cu_q + p.num_seqs)) return;  // grid covers all rows of q
     q_len = __ldg(p.cu_q + seq + 1) - __ldg(p.cu_q + seq);
     q_idx = (int)(row - __ldg(p.cu_q + seq));
   }

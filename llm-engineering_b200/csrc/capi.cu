@@ -28,11 +28,19 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 struct MapKey {
   const void* base;
-  int64_t layers, slots;
-  int heads, dim, elem;
+  int rank;
+  uint64_t dims[5];
+  uint64_t strides[4];
+  uint32_t box[5];
+  int dtype;
+  int swizzle;
   bool operator==(const MapKey& o) const {
-    return base == o.base && layers == o.layers && slots == o.slots && heads == o.heads &&
-           dim == o.dim && elem == o.elem;
+    if (base != o.base || rank != o.rank || dtype != o.dtype || swizzle != o.swizzle) return false;
+    for (int i = 0; i < 5; ++i)
+      if (dims[i] != o.dims[i] || box[i] != o.box[i]) return false;
+    for (int i = 0; i < 4; ++i)
+      if (strides[i] != o.strides[i]) return false;
+    return true;
   }
 };
 
@@ -42,10 +50,45 @@ struct MapEntry {
   bool used;
 };
 
-constexpr int kMapCache = 32;
+constexpr int kMapCache = 64;
 MapEntry g_maps[kMapCache];
 int g_next_victim = 0;
 std::mutex g_map_mutex;
+
+// Encode (or fetch from the cache) a tiled tensor map with 128-byte swizzle.
+int encode_cached(CUtensorMap* out, const MapKey& key) {
+  std::lock_guard<std::mutex> lock(g_map_mutex);
+  for (auto& e : g_maps) {
+    if (e.used && e.key == key) {
+      *out = e.map;
+      return B2P_OK;
+    }
+  }
+  auto fn = encode_fn();
+  if (fn == nullptr) return B2P_EDRIVER;
+  cuuint64_t dims[5];
+  cuuint64_t strides[4];
+  cuuint32_t box[5];
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  for (int i = 0; i < 5; ++i) {
+    dims[i] = key.dims[i];
+    box[i] = key.box[i];
+  }
+  for (int i = 0; i < 4; ++i) strides[i] = key.strides[i];
+  CUtensorMap map;
+  CUresult r = fn(&map, static_cast<CUtensorMapDataType>(key.dtype), key.rank,
+                  const_cast<void*>(key.base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, static_cast<CUtensorMapSwizzle>(key.swizzle),
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return B2P_EDRIVER;
+  MapEntry& victim = g_maps[g_next_victim];
+  g_next_victim = (g_next_victim + 1) % kMapCache;
+  victim.key = key;
+  victim.map = map;
+  victim.used = true;
+  *out = map;
+  return B2P_OK;
+}
 
 }  // namespace
 
@@ -79,50 +122,71 @@ int sm_count() {
   return counts[dev];
 }
 
-int pool_tensor_map(CUtensorMap* out, const void* base, int64_t num_layers, int64_t num_slots,
-                    int num_kv_heads, int head_dim, int elem_bytes) {
-  MapKey key{base, num_layers, num_slots, num_kv_heads, head_dim, elem_bytes};
-  std::lock_guard<std::mutex> lock(g_map_mutex);
-  for (auto& e : g_maps) {
-    if (e.used && e.key == key) {
-      *out = e.map;
-      return B2P_OK;
-    }
-  }
-  auto fn = encode_fn();
-  if (fn == nullptr) return B2P_EDRIVER;
+// 5-D map over a pool tensor [num_layers, num_slots, num_kv_heads, head_dim] with the box
+// {128-byte line, box_chunks lines, 1 head, 16 slots, 1 layer}.
+int pool_tensor_map_box(CUtensorMap* out, const void* base, int64_t num_layers, int64_t num_slots,
+                        int num_kv_heads, int head_dim, int elem_bytes, int box_chunks) {
   const int inner = 128 / elem_bytes;  // elements per 128-byte swizzle line
-  if (head_dim % inner != 0) return B2P_EUNSUPPORTED;
+  if (head_dim % inner != 0 || box_chunks < 1 || box_chunks > head_dim / inner)
+    return B2P_EUNSUPPORTED;
   const uint64_t es = static_cast<uint64_t>(elem_bytes);
-  cuuint64_t dims[5] = {static_cast<cuuint64_t>(inner),
-                        static_cast<cuuint64_t>(head_dim / inner),
-                        static_cast<cuuint64_t>(num_kv_heads),
-                        static_cast<cuuint64_t>(num_slots),
-                        static_cast<cuuint64_t>(num_layers)};
-  // Byte strides of dims 1..4 (dim 0 is the contiguous one).
-  cuuint64_t strides[4] = {static_cast<cuuint64_t>(inner * es),
-                           static_cast<cuuint64_t>(head_dim * es),
-                           static_cast<cuuint64_t>(num_kv_heads) * head_dim * es,
-                           static_cast<cuuint64_t>(num_slots) * num_kv_heads * head_dim * es};
-  cuuint32_t box[5] = {static_cast<cuuint32_t>(inner), static_cast<cuuint32_t>(head_dim / inner),
-                       1u, 16u, 1u};
-  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  MapKey k{};
+  k.base = base;
+  k.rank = 5;
+  k.dims[0] = inner;
+  k.dims[1] = head_dim / inner;
+  k.dims[2] = num_kv_heads;
+  k.dims[3] = num_slots;
+  k.dims[4] = num_layers;
+  k.strides[0] = inner * es;
+  k.strides[1] = head_dim * es;
+  k.strides[2] = static_cast<uint64_t>(num_kv_heads) * head_dim * es;
+  k.strides[3] = static_cast<uint64_t>(num_slots) * num_kv_heads * head_dim * es;
+  k.box[0] = inner;
+  k.box[1] = box_chunks;
+  k.box[2] = 1;
+  k.box[3] = 16;
+  k.box[4] = 1;
   // TMA tile loads copy bytes without conversion, so an unsigned type of the element
   // width serves bf16, f16 and f32 alike.
-  CUtensorMapDataType dt = elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16
-                                           : CU_TENSOR_MAP_DATA_TYPE_UINT32;
-  CUtensorMap map;
-  CUresult r = fn(&map, dt, 5, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return B2P_EDRIVER;
-  MapEntry& victim = g_maps[g_next_victim];
-  g_next_victim = (g_next_victim + 1) % kMapCache;
-  victim.key = key;
-  victim.map = map;
-  victim.used = true;
-  *out = map;
-  return B2P_OK;
+  k.dtype = elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32;
+  k.swizzle = CU_TENSOR_MAP_SWIZZLE_128B;
+  return encode_cached(out, k);
+}
+
+int pool_tensor_map(CUtensorMap* out, const void* base, int64_t num_layers, int64_t num_slots,
+                    int num_kv_heads, int head_dim, int elem_bytes) {
+  return pool_tensor_map_box(out, base, num_layers, num_slots, num_kv_heads, head_dim, elem_bytes,
+                             head_dim / (128 / elem_bytes));
+}
+
+// 4-D map over token-major activations [rows, heads, head_dim] (element strides given)
+// with the box {128-byte line, 1 line, 1 head, box_rows rows}.
+int tensor_map_4d_rows(CUtensorMap* out, const void* base, int64_t rows, int heads, int head_dim,
+                       int64_t row_stride_elems, int64_t head_stride_elems, int elem_bytes,
+                       int box_rows) {
+  const int inner = 128 / elem_bytes;
+  if (head_dim % inner != 0 || rows <= 0) return B2P_EUNSUPPORTED;
+  const uint64_t es = static_cast<uint64_t>(elem_bytes);
+  MapKey k{};
+  k.base = base;
+  k.rank = 4;
+  k.dims[0] = inner;
+  k.dims[1] = head_dim / inner;
+  k.dims[2] = heads;
+  k.dims[3] = rows;
+  k.dims[4] = 1;
+  k.strides[0] = inner * es;
+  k.strides[1] = head_stride_elems * es;
+  k.strides[2] = row_stride_elems * es;
+  k.box[0] = inner;
+  k.box[1] = 1;
+  k.box[2] = 1;
+  k.box[3] = box_rows;
+  k.box[4] = 1;
+  k.dtype = elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32;
+  k.swizzle = CU_TENSOR_MAP_SWIZZLE_128B;
+  return encode_cached(out, k);
 }
 
 }  // namespace b2p_host

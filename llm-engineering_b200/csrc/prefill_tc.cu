@@ -1,0 +1,600 @@
+// K3 — packed variable-length causal prefill / chunked-prefill attention on tcgen05.
+//
+// Reference path replaced (PREFILL executions): HFBatchedPagedCache.update gathers every
+// history (serving/engine/hf_batched_paged_cache.py:52-148), build_attention_mask adds a
+// dense tril block per prefill (serving/engine/attention_mask.py:37-45) and HF SDPA runs
+// over all packed keys (transformers/integrations/sdpa_attention.py:40-104). Here each CTA
+// computes one tile of 128 query rows of one (sequence, query head) against the sequence's
+// keys read in place from the paged pool:
+//
+//   S = Q K^T   tcgen05.mma kind::f16, A = Q (smem, K-major), B = K tile (smem, K-major),
+//               D = S in tensor memory (fp32, 128 lanes x 64 columns, two buffers)
+//   P = softmax rows of S, one thread per query row (tcgen05.ld -> fp32 -> exp2), written
+//       back as bf16/f16 over its own S buffer (tcgen05.st)
+//   O += P V    tcgen05.mma with A = P from tensor memory, B = V tile (smem, MN-major),
+//               D = O in tensor memory (fp32, 128 x head_dim)
+//
+// K/V tiles of 64 tokens are assembled from four 16-slot pool sub-blocks (TMA tile loads,
+// 128-byte swizzle, no multicast) into a two-stage ring. A query row j of sequence i sits
+// at position ctx_i - q_len_i + j and sees keys 0..position (whole-history prefill when
+// q_len == ctx, chunked prefill otherwise). The running max is only moved (and O rescaled)
+// when a row's max grows by more than 2^8, so exp2 values stay below 256 and the O
+// correction is rare.
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = tensor-memory owner and MMA
+// issuer (one thread), warps 2..5 = softmax + epilogue (thread = TMEM lane = query row).
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace {
+
+using namespace b2p;
+
+constexpr int kM = 128;     // query rows per tile
+constexpr int kN = 64;      // keys per KV tile
+constexpr int kD = 128;     // head_dim handled by this kernel
+constexpr int kThreads = 192;
+constexpr int kSub = 16;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+struct PrefillParams {
+  const int32_t* block_tables;
+  int64_t bt_stride;
+  const int32_t* cu_q;
+  const int32_t* ctx;
+  int num_seqs;
+  int group;
+  int layer;
+  int block_size;
+  int64_t num_blocks;
+  float scale_log2;
+  uint8_t* out;
+  int64_t o_tok, o_head;
+  int32_t* err;
+};
+
+// Shared-memory plan (bytes from the 1024-aligned base).
+constexpr int kQBytes = 2 * kM * 128;        // 2 chunks x 128 rows x 128 B
+constexpr int kKVBytes = 2 * kN * 128;       // 2 chunks x 64 rows x 128 B
+constexpr int kOffQ = 0;
+constexpr int kOffK = kOffQ + kQBytes;       // 2 stages
+constexpr int kOffV = kOffK + 2 * kKVBytes;  // 2 stages
+constexpr int kOffBar = kOffV + 2 * kKVBytes;
+constexpr int kNumBars = 1 + 2 * 6;          // q_full, k_full[2], v_full[2], kv_empty[2],
+                                             // s_full[2], p_full[2], o_done[2]
+constexpr int kOffMisc = kOffBar + kNumBars * 8 + 8;  // + mma_done
+constexpr int kSmemBytes = kOffMisc + 64;
+
+// TMEM columns: S buffers at 0 and 64, O at 128 (256 allocated).
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kColS0 = 0, kColS1 = 64, kColO = 128;
+
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;  // 128-byte swizzle
+  return d;
+}
+
+// kind::f16 instruction descriptor: fp32 accumulate, A/B of `ab` format (0 = f16,
+// 1 = bf16), A/B major (0 = K-major, 1 = MN-major), M x N.
+__device__ __forceinline__ uint32_t idesc_f16(uint32_t ab, int m, int n, uint32_t a_mn,
+                                              uint32_t b_mn) {
+  return (1u << 4) | (ab << 7) | (ab << 10) | (a_mn << 15) | (b_mn << 16) |
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+#define B2P_R32(v)                                                                        \
+  "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),    \
+      "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),          \
+      "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),       \
+      "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),       \
+      "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+#define B2P_W32(v)                                                                        \
+  "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), \
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),   \
+      "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), \
+      "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), \
+      "r"(v[29]), "r"(v[30]), "r"(v[31])
+
+// 32 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : B2P_R32(v)
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+      "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(
+          taddr),
+      B2P_W32(v));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map,
+                                            uint64_t* bar, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];\n" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
+      "r"(c3)
+      : "memory");
+}
+
+__device__ __forceinline__ int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+// Work item k -> (sequence, query tile), tiles of a sequence enumerated last first (the
+// last tiles see the most keys, so they start early). One warp; all lanes return it.
+__device__ bool find_item(const PrefillParams& p, int k, int& seq, int& tile) {
+  const int lane = threadIdx.x & 31;
+  int run = 0;
+  for (int base = 0; base < p.num_seqs; base += 32) {
+    const int i = base + lane;
+    int nt = 0;
+    if (i < p.num_seqs) nt = ceil_div(max(__ldg(p.cu_q + i + 1) - __ldg(p.cu_q + i), 0), kM);
+    int incl = nt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const unsigned hit = __ballot_sync(0xffffffffu, run + incl > k);
+    if (hit) {
+      const int src = __ffs(hit) - 1;
+      const int lo = run + __shfl_sync(0xffffffffu, incl - nt, src);
+      const int cnt = __shfl_sync(0xffffffffu, nt, src);
+      seq = base + src;
+      tile = cnt - 1 - (k - lo);
+      return true;
+    }
+    run += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  return false;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_constant__ CUtensorMap qmap,
+                                                                const __grid_constant__ CUtensorMap kmap,
+                                                                const __grid_constant__ CUtensorMap vmap,
+                                                                const PrefillParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = bars + 3;
+  uint64_t* kv_empty = bars + 5;
+  uint64_t* s_full = bars + 7;
+  uint64_t* p_full = bars + 9;
+  uint64_t* o_done = bars + 11;
+  uint64_t* mma_done = bars + 13;
+  int32_t* misc = reinterpret_cast<int32_t*>(smem + kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 5);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int qh = blockIdx.y;
+  const int kvh = qh / p.group;
+
+  if (warp == 0) {
+    int seq = -1, tile = 0;
+    const bool ok = find_item(p, (int)blockIdx.x, seq, tile);
+    if (lane == 0) {
+      misc[0] = ok ? seq : -1;
+      misc[1] = tile;
+      *abort_flag = 0;
+      if (ok) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < 2; ++s) {
+          mbar_init(&k_full[s], 1);
+          mbar_init(&v_full[s], 1);
+          mbar_init(&kv_empty[s], 1);
+          mbar_init(&s_full[s], 1);
+          mbar_init(&p_full[s], kM);
+          mbar_init(&o_done[s], 1);
+        }
+        mbar_init(mma_done, 1);
+        fence_mbar_init();
+      }
+    }
+  }
+  __syncthreads();
+  const int seq = misc[0];
+  if (seq < 0) return;  // grid is an upper bound on the number of tiles
+  const int qt = misc[1];
+  const int q0 = __ldg(p.cu_q + seq);
+  const int qlen = __ldg(p.cu_q + seq + 1) - q0;
+  const int ctx = __ldg(p.ctx + seq);
+  const int rows_valid = min(kM, qlen - qt * kM);
+  const int pos0 = ctx - qlen + qt * kM;            // position of the tile's first row
+  const int last_pos = pos0 + rows_valid - 1;
+  const int n_kv = last_pos >= 0 ? ceil_div(last_pos + 1, kN) : 0;
+  if (threadIdx.x == 0 && (ctx < qlen || n_kv == 0)) set_device_error(p.err, B2P_DEV_LENGTH);
+  const uint32_t ab = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+
+  if (warp == 1) {  // tensor memory for S0, S1, O
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    const int spb = p.block_size / kSub;
+    const int64_t num_slots = p.num_blocks * p.block_size;
+    const int32_t* bt = p.block_tables + (int64_t)seq * p.bt_stride;
+    if (lane == 0) {
+      tma_prefetch_desc(&qmap);
+      tma_prefetch_desc(&kmap);
+      tma_prefetch_desc(&vmap);
+      mbar_arrive_expect_tx(q_full, kQBytes);
+      for (int c = 0; c < 2; ++c)
+        tma_load_4d(smem + kOffQ + c * (kM * 128), &qmap, q_full, 0, c, qh, q0 + qt * kM);
+    }
+    // lane l holds the slot of sub-block (win + l); 8 KV tiles per window
+    int win = -32;
+    int64_t my_slot = 0;
+    bool aborted = false;
+    int last_issued = -1;
+    for (int j = 0; j < n_kv && !aborted; ++j) {
+      const int s = j & 1;
+      if (j * 4 >= win + 32) {
+        win = j * 4;
+        const int sb = win + lane;  // sub-block index within the sequence
+        const int64_t col = sb / spb;
+        int32_t blk = -1;
+        if ((int64_t)sb * kSub < ctx && col < p.bt_stride) blk = __ldg(bt + col);
+        if ((int64_t)sb * kSub < ctx && (blk < 0 || (int64_t)blk >= p.num_blocks)) {
+          set_device_error(p.err, B2P_DEV_BLOCK_RANGE);
+          blk = -1;
+        }
+        my_slot = blk < 0 ? num_slots : (int64_t)blk * p.block_size + (int64_t)(sb % spb) * kSub;
+      }
+      int64_t slots[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) slots[u] = __shfl_sync(0xffffffffu, my_slot, j * 4 - win + u);
+      if (lane == 0) {
+        if (j >= 2 && !mbar_wait_bounded(&kv_empty[s], (uint32_t)(((j >> 1) - 1) & 1), p.err)) {
+          *abort_flag = 1;
+          aborted = true;
+        } else if (*abort_flag) {
+          aborted = true;
+        } else {
+          uint8_t* kdst = smem + kOffK + s * kKVBytes;
+          uint8_t* vdst = smem + kOffV + s * kKVBytes;
+          mbar_arrive_expect_tx(&k_full[s], kKVBytes);
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+              tma_load_5d(kdst + c * (kN * 128) + u * (kSub * 128), &kmap, &k_full[s], 0, c, kvh,
+                          (int)slots[u], p.layer);
+          mbar_arrive_expect_tx(&v_full[s], kKVBytes);
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+              tma_load_5d(vdst + c * (kN * 128) + u * (kSub * 128), &vmap, &v_full[s], 0, c, kvh,
+                          (int)slots[u], p.layer);
+          last_issued = j;
+        }
+      }
+      aborted = __shfl_sync(0xffffffffu, aborted ? 1 : 0, 0) != 0;
+    }
+    if (lane == 0) misc[2] = last_issued;
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0 && n_kv > 0) {
+      const uint32_t id_qk = idesc_f16(ab, kM, kN, 0, 0);
+      const uint32_t id_pv = idesc_f16(ab, kM, kD, 0, 1);
+      const uint32_t q_addr = smem_u32(smem + kOffQ);
+      bool ok = mbar_wait_bounded(q_full, 0, p.err);
+      auto issue_qk = [&](int j) {
+        const int s = j & 1;
+        const uint32_t k_addr = smem_u32(smem + kOffK + s * kKVBytes);
+        const uint32_t d = tbase + (s ? kColS1 : kColS0);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint64_t da = smem_desc_sw128(q_addr + (kk >> 2) * (kM * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t db = smem_desc_sw128(k_addr + (kk >> 2) * (kN * 128) + (kk & 3) * 32, 16, 1024);
+          mma_ss(d, da, db, id_qk, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&s_full[s]);
+      };
+      if (ok) ok = mbar_wait_bounded(&k_full[0], 0, p.err);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(0);
+      }
+      for (int j = 0; j < n_kv && ok && !*abort_flag; ++j) {
+        const int s = j & 1;
+        if (j + 1 < n_kv) {
+          const int s1 = (j + 1) & 1;
+          // S buffer s1 held P(j-1): PV(j-1) must be done reading it.
+          if (j >= 1) ok = mbar_wait_bounded(&o_done[(j - 1) & 1], (uint32_t)(((j - 1) >> 1) & 1), p.err);
+          if (ok) ok = mbar_wait_bounded(&k_full[s1], (uint32_t)(((j + 1) >> 1) & 1), p.err);
+          if (!ok) break;
+          tc_fence_after();
+          issue_qk(j + 1);
+        }
+        ok = mbar_wait_bounded(&p_full[s], (uint32_t)((j >> 1) & 1), p.err);
+        if (ok) ok = mbar_wait_bounded(&v_full[s], (uint32_t)((j >> 1) & 1), p.err);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(smem + kOffV + s * kKVBytes);
+        const uint32_t p_tmem = tbase + (s ? kColS1 : kColS0);
+#pragma unroll
+        for (int kk = 0; kk < kN / 16; ++kk) {
+          const uint64_t db = smem_desc_sw128(v_addr + kk * (16 * 128), kN * 128, 1024);
+          mma_ts(tbase + kColO, p_tmem + kk * 8, db, id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(&kv_empty[s]);
+        mma_commit(&o_done[s]);
+      }
+      if (!ok) *abort_flag = 1;
+      // every MMA issued above has completed once this commit arrives
+      mma_commit(mma_done);
+      mbar_wait_bounded(mma_done, 0, nullptr);
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax + epilogue
+    const int quarter = warp & 3;        // TMEM lanes 32*quarter .. +31
+    const int row = quarter * 32 + lane;  // query row within the tile
+    const uint32_t lane_base = tbase + ((uint32_t)(quarter * 32) << 16);
+    const bool valid_row = row < rows_valid;
+    const int pos = pos0 + row;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int s = j & 1;
+      if (ok && !mbar_wait_bounded(&s_full[s], (uint32_t)((j >> 1) & 1), p.err)) ok = false;
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || *abort_flag) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t s_col = lane_base + (s ? kColS1 : kColS0);
+      uint32_t r0[32], r1[32];
+      tmem_ld32(s_col, r0);
+      tmem_ld32(s_col + 32, r1);
+      tmem_wait_ld();
+      const int key0 = j * kN;
+      // key c of this tile is visible iff key0 + c <= pos (then also < ctx)
+      const int nvis = valid_row ? min(kN, pos - key0 + 1) : 0;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        if (c < nvis) mx = fmaxf(mx, __uint_as_float(r0[c]));
+        if (32 + c < nvis) mx = fmaxf(mx, __uint_as_float(r1[c]));
+      }
+      mx = mx * p.scale_log2;  // scale_log2 > 0 keeps the arg-max
+      bool rescale = false;
+      float alpha = 1.f;
+      if (mx > -INFINITY) {
+        if (m == -INFINITY) {
+          m = mx;
+        } else if (mx > m + kRescaleThreshold) {
+          alpha = fast_exp2(m - mx);
+          m = mx;
+          rescale = true;
+        }
+      }
+      // Rows that move their reference max fix O once PV(j-1) has landed.
+      if (__any_sync(0xffffffffu, rescale)) {
+        if (!mbar_wait_bounded(&o_done[(j - 1) & 1], (uint32_t)(((j - 1) >> 1) & 1), p.err)) ok = false;
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        for (int c0 = 0; c0 < kD; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32(lane_base + kColO + c0, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+          tmem_st32(lane_base + kColO + c0, o);
+        }
+        tmem_wait_st();
+        l *= alpha;
+      }
+      uint32_t pk[32];
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {  // tokens 0..31 from r0, 32..63 from r1
+        const float e0 = 2 * c < nvis ? fast_exp2(__uint_as_float(r0[2 * c]) * p.scale_log2 - m) : 0.f;
+        const float e1 = 2 * c + 1 < nvis ? fast_exp2(__uint_as_float(r0[2 * c + 1]) * p.scale_log2 - m) : 0.f;
+        const float e2 = 32 + 2 * c < nvis ? fast_exp2(__uint_as_float(r1[2 * c]) * p.scale_log2 - m) : 0.f;
+        const float e3 = 33 + 2 * c < nvis ? fast_exp2(__uint_as_float(r1[2 * c + 1]) * p.scale_log2 - m) : 0.f;
+        rs += (e0 + e1) + (e2 + e3);
+        pk[c] = pack2<T>(e0, e1);
+        pk[16 + c] = pack2<T>(e2, e3);
+      }
+      l += rs;
+      tmem_st32(s_col, pk);
+      tmem_wait_st();
+      // Keys past the context (the last KV tile's tail) may hold NaN/Inf in the pool;
+      // P is 0 there but 0 * NaN is not: zero those V rows before the PV MMA reads them.
+      const int tail0 = ctx - key0;  // first row of this tile past the context
+      if (j == n_kv - 1 && tail0 < kN) {
+        if (!mbar_wait_bounded(&v_full[s], (uint32_t)((j >> 1) & 1), p.err)) ok = false;
+        uint8_t* vt = smem + kOffV + s * kKVBytes;
+        const int zrows = kN - max(tail0, 0);
+        for (int e = threadIdx.x - 64; e < 2 * zrows * 8; e += 128) {
+          const int c = e / (zrows * 8);         // d chunk
+          const int rem = e - c * zrows * 8;
+          const int r = max(tail0, 0) + rem / 8;  // token row
+          const int q16 = rem % 8;                // 16-byte piece of the 128-byte line
+          reinterpret_cast<uint4*>(vt + c * (kN * 128) + r * 128)[q16] = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+      }
+      tc_fence_before();
+      mbar_arrive(&p_full[s]);
+    }
+    // ---- epilogue: O / l -> out
+    if (ok && n_kv > 0) {
+      const int jl = n_kv - 1;
+      if (!mbar_wait_bounded(&o_done[jl & 1], (uint32_t)((jl >> 1) & 1), p.err)) ok = false;
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (ok && n_kv > 0) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      T* orow = reinterpret_cast<T*>(p.out) + (int64_t)(q0 + qt * kM + row) * p.o_tok +
+                (int64_t)qh * p.o_head;
+      for (int c0 = 0; c0 < kD; c0 += 32) {
+        uint32_t o[32];
+        tmem_ld32(lane_base + kColO + c0, o);
+        tmem_wait_ld();
+        if (valid_row) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int c = 0; c < 16; ++c)
+            pk[c] = pack2<T>(__uint_as_float(o[2 * c]) * inv, __uint_as_float(o[2 * c + 1]) * inv);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            reinterpret_cast<uint4*>(orow + c0)[c] = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        }
+      }
+    }
+    if (!ok) *abort_flag = 1;
+  }
+
+  // ---- teardown: every TMA and MMA of this CTA has finished before TMEM is freed
+  if (warp == 0 && lane == 0) {
+    // Q always lands before the CTA leaves; after an abort, so do the last two K/V tiles
+    // the producer issued.
+    mbar_wait_bounded(q_full, 0, nullptr);
+    if (*abort_flag) {
+      const int last = misc[2];
+      for (int j = max(0, last - 1); j <= last; ++j) {
+        mbar_wait_bounded(&k_full[j & 1], (uint32_t)((j >> 1) & 1), nullptr);
+        mbar_wait_bounded(&v_full[j & 1], (uint32_t)((j >> 1) & 1), nullptr);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase),
+                 "r"(kTmemCols));
+}
+
+}  // namespace
+
+// ====================================================================== host side
+namespace b2p_host {
+int tensor_map_4d_rows(CUtensorMap* out, const void* base, int64_t rows, int heads, int head_dim,
+                       int64_t row_stride_elems, int64_t head_stride_elems, int elem_bytes,
+                       int box_rows);
+int pool_tensor_map_box(CUtensorMap* out, const void* base, int64_t num_layers, int64_t num_slots,
+                        int num_kv_heads, int head_dim, int elem_bytes, int box_chunks);
+}  // namespace b2p_host
+
+// Launches the tcgen05 prefill when the shape allows it; returns B2P_EUNSUPPORTED otherwise
+// (the caller then runs the CUDA-core kernel).
+int b2p_prefill_tc(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
+                   const void* key_cache, const void* value_cache, int64_t layer_index,
+                   int64_t num_layers, int64_t num_slots, const int32_t* block_tables,
+                   int64_t block_table_stride, const int32_t* cu_seqlens_q,
+                   const int32_t* context_lens, int num_seqs, int64_t total_q, int num_q_heads,
+                   int num_kv_heads, int head_dim, int block_size, float scale, void* out,
+                   int64_t out_tok_stride, int64_t out_head_stride, int dtype, int32_t* err_flag,
+                   void* stream) {
+  if (head_dim != kD || (dtype != B2P_BF16 && dtype != B2P_F16) || block_size % kSub != 0)
+    return B2P_EUNSUPPORTED;
+  auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
+  if (!al16(q) || !al16(out) || !al16(key_cache) || !al16(value_cache) ||
+      (q_tok_stride * 2) % 16 || (q_head_stride * 2) % 16 || (out_tok_stride * 2) % 16 ||
+      (out_head_stride * 2) % 16 || num_slots > 0x7fffffffLL || total_q > 0x7fffffffLL)
+    return B2P_EUNSUPPORTED;
+  CUtensorMap qmap, kmap, vmap;
+  int rc = b2p_host::tensor_map_4d_rows(&qmap, q, total_q, num_q_heads, head_dim, q_tok_stride,
+                                        q_head_stride, 2, kM);
+  if (rc != B2P_OK) return rc;
+  rc = b2p_host::pool_tensor_map_box(&kmap, key_cache, num_layers, num_slots, num_kv_heads,
+                                     head_dim, 2, 1);
+  if (rc != B2P_OK) return rc;
+  rc = b2p_host::pool_tensor_map_box(&vmap, value_cache, num_layers, num_slots, num_kv_heads,
+                                     head_dim, 2, 1);
+  if (rc != B2P_OK) return rc;
+  PrefillParams p;
+  p.block_tables = block_tables;
+  p.bt_stride = block_table_stride;
+  p.cu_q = cu_seqlens_q;
+  p.ctx = context_lens;
+  p.num_seqs = num_seqs;
+  p.group = num_q_heads / num_kv_heads;
+  p.layer = (int)layer_index;
+  p.block_size = block_size;
+  p.num_blocks = num_slots / block_size;
+  p.scale_log2 = scale * kLog2e;
+  p.out = static_cast<uint8_t*>(out);
+  p.o_tok = out_tok_stride;
+  p.o_head = out_head_stride;
+  p.err = err_flag;
+  const void* fn = dtype == B2P_BF16
+                       ? reinterpret_cast<const void*>(&paged_prefill_tc<__nv_bfloat16>)
+                       : reinterpret_cast<const void*>(&paged_prefill_tc<__half>);
+  const int smem = kSmemBytes + 1024;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return b2p_host::record_error(e);
+  // Upper bound on the number of 128-row tiles: sum(ceil(q_len / 128)) <= seqs + rows / 128.
+  const int64_t tiles = (int64_t)num_seqs + total_q / kM + 1;
+  if (tiles > 0x7fffffffLL) return B2P_EUNSUPPORTED;
+  dim3 grid((unsigned)tiles, (unsigned)num_q_heads);
+  void* args[] = {&qmap, &kmap, &vmap, &p};
+  e = cudaLaunchKernel(fn, grid, dim3(kThreads), args, (size_t)smem,
+                       static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return b2p_host::record_error(e);
+  return b2p_host::check_launch();
+}

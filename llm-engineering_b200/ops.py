@@ -168,13 +168,12 @@ def paged_prefill(
     scale: float,
     out: torch.Tensor | None = None,
     err_flag: torch.Tensor | None = None,
-    num_rows: int | None = None,
 ) -> torch.Tensor:
     """K3: packed variable-length causal attention over the paged history.
 
     q: (rows, num_q_heads, head_dim); sequence i owns rows [cu_seqlens_q[i],
-    cu_seqlens_q[i+1]) of q (int32, num_seqs + 1 entries, need not start at 0).
-    num_rows = cu_seqlens_q[-1] - cu_seqlens_q[0] (defaults to all rows of q).
+    cu_seqlens_q[i+1]) of q (int32, num_seqs + 1 entries, need not start at 0, so a
+    trailing slice of a packed batch can be run with views of its metadata).
     """
     _check_pool(key_cache, value_cache)
     _require_cuda("q", q)
@@ -193,8 +192,7 @@ def paged_prefill(
     rc = _lib.load().b2p_paged_prefill(
         q.data_ptr(), qt, qhs, key_cache.data_ptr(), value_cache.data_ptr(), layer_index, layers,
         slots, block_tables.data_ptr(), block_tables.stride(0), cu_seqlens_q.data_ptr(),
-        context_lens.data_ptr(), num_seqs, total_q if num_rows is None else num_rows, max_q_len,
-        hq, hkv, d, block_size,
+        context_lens.data_ptr(), num_seqs, total_q, max_q_len, hq, hkv, d, block_size,
         float(scale), out.data_ptr(), ot, ohs, dtype_code(q.dtype), _ptr(err_flag),
         _stream(q.device),
     )

@@ -108,8 +108,7 @@ def paged_attention(module: torch.nn.Module, query: torch.Tensor, key: torch.Ten
     if nd < batch.num_execs:
         k.paged_prefill(q, batch.key_cache, batch.value_cache, layer, batch.block_tables[nd:],
                         batch.cu_seqlens_q[nd:], batch.context_lens[nd:], batch.max_q_len,
-                        batch.block_size, scaling, out=out, err_flag=batch.err,
-                        num_rows=batch.total_q - nd)
+                        batch.block_size, scaling, out=out, err_flag=batch.err)
     return out.unsqueeze(0), None
 
 

@@ -271,3 +271,54 @@ def test_metadata_bit_exact(ops):
     bt = md["block_tables"].cpu().numpy()
     for i, t in enumerate(tables):
         assert bt[i, :len(t)].tolist() == t and (bt[i, len(t):] == -1).all()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_prefill_tensor_core_long_prompts_and_chunks(ops, dtype):
+    """Prompts up to 2,100 tokens (several 128-row tiles, many 64-key tiles), fragmented
+    blocks, whole-history and chunked runs, NaN in the pool slots past every context."""
+    hq, hkv, d, bs = 12, 2, 128, 16
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(80)
+    ctx = [2100, 64, 129, 1000, 777, 300, 16]
+    qlen = [2100, 64, 129, 1000, 200, 1, 16]
+    cu = np.concatenate([[0], np.cumsum(qlen)]).tolist()
+    nb = sum((c + bs - 1) // bs for c in ctx) + 5
+    kc, vc = make_pool(81, 1, nb, bs, hkv, d, dtype)
+    tables, bt = make_tables(82, ctx, bs, nb)
+    for t, c in zip(tables, ctx):
+        tail = c % bs
+        if tail:
+            kc[0, t[-1] * bs + tail:(t[-1] + 1) * bs] = float("nan")
+            vc[0, t[-1] * bs + tail:(t[-1] + 1) * bs] = float("nan")
+    q = torch.randn(cu[-1], hq, d, generator=torch.Generator().manual_seed(83)).to(dtype)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = ops.paged_prefill(q.to(dev), kc.to(dev), vc.to(dev), 0, bt.to(dev),
+                            torch.tensor(cu, dtype=torch.int32, device=dev),
+                            torch.tensor(ctx, dtype=torch.int32, device=dev), max(qlen), bs,
+                            d ** -0.5, err_flag=err)
+    assert int(err.item()) == 0
+    assert torch.isfinite(out.float()).all()
+    close(out, ref.prefill_attention(q, kc, vc, 0, tables, cu, ctx, bs, d ** -0.5), dtype)
+
+
+def test_prefill_trailing_slice_of_packed_batch(ops):
+    """The runner's call: decode rows first, prefill rows run with views of the metadata."""
+    hq, hkv, d, bs = 12, 2, 128, 16
+    dev = torch.device("cuda")
+    ctx = [50, 33, 300, 140]
+    qlen = [1, 1, 300, 12]
+    cu = np.concatenate([[0], np.cumsum(qlen)]).tolist()
+    nb = sum((c + bs - 1) // bs for c in ctx) + 2
+    kc, vc = make_pool(90, 1, nb, bs, hkv, d, torch.bfloat16)
+    tables, bt = make_tables(91, ctx, bs, nb)
+    q = torch.randn(cu[-1], hq, d, generator=torch.Generator().manual_seed(92)).to(torch.bfloat16)
+    cu_d = torch.tensor(cu, dtype=torch.int32, device=dev)
+    ctx_d = torch.tensor(ctx, dtype=torch.int32, device=dev)
+    bt_d = bt.to(dev)
+    out = torch.zeros(cu[-1], hq, d, dtype=torch.bfloat16, device=dev)
+    ops.paged_prefill(q.to(dev), kc.to(dev), vc.to(dev), 0, bt_d[2:], cu_d[2:], ctx_d[2:], 300, bs,
+                      d ** -0.5, out=out)
+    expect = ref.prefill_attention(q, kc, vc, 0, tables[2:], cu[2:], ctx[2:], bs, d ** -0.5)
+    close(out[2:], expect, torch.bfloat16)
+    assert torch.count_nonzero(out[:2].float()) == 0  # decode rows untouched
