@@ -121,6 +121,31 @@ B2P_API int b2p_paged_decode(const void* q, int64_t q_tok_stride, int64_t q_head
                      void* stream);
 
 /*
+ * K2 without caller-provided scratch. No counterpart in the reference (its PyTorch path
+ * has no scratch to provide). Same arguments and results as b2p_paged_decode minus the
+ * workspace: the split-K counters and partial records live in a 16 MiB array compiled
+ * into this library (kept by every GPU that loads it until the process exits). Meant for
+ * callers that cannot allocate device memory for the library, such as a runtime whose
+ * device memory is all reserved by its own arena, or a binding from a language that has
+ * no device allocator of its own.
+ *   - The first call on a device looks up the array's device address (with that device
+ *     current); make that first call before any stream capture.
+ *   - Every call clears the counters on `stream` and reuses the same array, so calls whose
+ *     work overlaps on the GPU (other streams, other threads) race: serialise them.
+ *   - Returns B2P_EWORKSPACE, launching nothing, when the problem needs more than the
+ *     array holds.
+ *   - Allocates nothing (no cudaMalloc / cudaFree).
+ */
+B2P_API int b2p_paged_decode_noalloc(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
+                                     const void* key_cache, const void* value_cache,
+                                     int64_t layer_index, int64_t num_layers, int64_t num_slots,
+                                     const int32_t* block_tables, int64_t block_table_stride,
+                                     const int32_t* context_lens, int num_seqs, int num_q_heads,
+                                     int num_kv_heads, int head_dim, int block_size, float scale,
+                                     void* out, int64_t out_tok_stride, int64_t out_head_stride,
+                                     int dtype, int32_t* err_flag, void* stream);
+
+/*
  * K3 — packed variable-length causal attention (prefill and chunked prefill) over the
  * paged pool. Replaces, for PREFILL executions, the same reference steps as K2 plus the
  * causal tril blocks of build_attention_mask (serving/engine/attention_mask.py:37-45).

@@ -29,6 +29,8 @@
 //    cut by range boundaries leaves an fp32 partial (O, running max, running sum) per warp
 //    in the workspace; once a warp's stream is done it counts its partials in (atomic
 //    counter per sequence) and the last warp to report a sequence merges its partials.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace {
@@ -850,4 +852,69 @@ extern "C" int b2p_paged_decode(const void* q, int64_t q_tok_stride, int64_t q_h
                                    static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return b2p_host::record_error(e);
   return b2p_host::check_launch();
+}
+
+// ====================================================================== scratch-free decode
+// Some callers cannot hand this library device scratch. Examples: a runtime that
+// reserves all device memory in its own arena at start-up and cannot carve out more,
+// and a language binding (Go, Java, Node) that drives these kernels without any device
+// allocator of its own. For them, the decode entry point below keeps the split-K
+// counters and partial records in a fixed array compiled into the library.
+namespace {
+
+// 16 MiB holds the counters and partial records of, for example, 256 sequences of a
+// 12/2-head, head_dim-128 layer (about 7.5 MiB on a 148-SM B200). Every GPU that loads
+// the library keeps this array until the process exits.
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+static __device__ __align__(256) uint8_t g_decode_scratch[kNoAllocScratchBytes];
+
+// Device address of g_decode_scratch on the current device (its host-side name is only
+// a stand-in, not a device pointer). Looked up once per device.
+int noalloc_scratch(void** ptr) {
+  static void* addr[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return b2p_host::record_error(e);
+  if (dev < 0 || dev >= 64) return B2P_EUNSUPPORTED;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess) return b2p_host::record_error(e);
+    addr[dev] = p;
+  }
+  *ptr = addr[dev];
+  return B2P_OK;
+}
+
+}  // namespace
+
+extern "C" int b2p_paged_decode_noalloc(const void* q, int64_t q_tok_stride,
+                                        int64_t q_head_stride, const void* key_cache,
+                                        const void* value_cache, int64_t layer_index,
+                                        int64_t num_layers, int64_t num_slots,
+                                        const int32_t* block_tables, int64_t block_table_stride,
+                                        const int32_t* context_lens, int num_seqs,
+                                        int num_q_heads, int num_kv_heads, int head_dim,
+                                        int block_size, float scale, void* out,
+                                        int64_t out_tok_stride, int64_t out_head_stride,
+                                        int dtype, int32_t* err_flag, void* stream) {
+  if (num_seqs < 0 || num_kv_heads <= 0) return B2P_EINVAL;
+  if (num_seqs == 0) return B2P_OK;
+  // The per-sequence counters alone must fit; the full requirement (which depends on the
+  // device's SM count) is checked against the array size by b2p_paged_decode below.
+  const size_t counters = counters_bytes(num_seqs, num_kv_heads);
+  if (counters > kNoAllocScratchBytes) return B2P_EWORKSPACE;
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc != B2P_OK) return rc;
+  // The array keeps whatever the previous call left; the counters must start at zero.
+  cudaError_t e = cudaMemsetAsync(scratch, 0, counters, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return b2p_host::record_error(e);
+  return b2p_paged_decode(q, q_tok_stride, q_head_stride, key_cache, value_cache, layer_index,
+                          num_layers, num_slots, block_tables, block_table_stride, context_lens,
+                          num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, scale, out,
+                          out_tok_stride, out_head_stride, scratch, kNoAllocScratchBytes, dtype,
+                          err_flag, stream);
 }
