@@ -208,6 +208,9 @@ def run_ours(args) -> None:
                                 device_id=dev)
     L = args.layers
     w = make_workload(1234 + rank, dev, layers=L)
+    if L == 1:  # make_workload drops the layer dimension of single-layer tensors
+        for key in ("q", "new_k", "new_v"):
+            w[key] = w[key].unsqueeze(0)
     kc, vc = w["kc"], w["vc"]
     q = w["q"].to(dev)
     new_k, new_v = w["new_k"].to(dev), w["new_v"].to(dev)
