@@ -47,9 +47,10 @@ import torch
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
-# Per-launch DRAM traffic of K2 on this workload from one ncu capture
-# (profiles/paged_decode_c2.md); None until captured.
-K2_TRAFFIC_BYTES: float | None = None
+# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of K2 on this
+# workload, from one ncu capture of a K2 launch over the same sequences and block tables
+# (profiles/paged_decode_tc_decode256.md): 616.06 MB read + 6.83 MB written.
+K2_TRAFFIC_BYTES: float | None = 622.887936e6
 
 NUM_SEQS = 256
 CTX_LO, CTX_HI = 512, 4096
