@@ -1,9 +1,8 @@
 // Shared device helpers for the sm_100a paged-attention kernels.
 //
 // Everything here is inline PTX for the Blackwell data path: mbarriers, TMA tiled
-// loads (cp.async.bulk.tensor, never with .multicast::cluster: the pool may live on a
-// GPU that other replicas never touch, and multicast loads are not used anywhere in
-// this library), ldmatrix/movmatrix and the m16n8k16 tensor-core MMA used by the
+// loads (cp.async.bulk.tensor into this CTA's own shared memory only; no load in this
+// library is shared across a cluster), ldmatrix/movmatrix and the m16n8k16 tensor-core MMA used by the
 // decode kernel for its tiny per-block contractions.
 #pragma once
 
