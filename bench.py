@@ -393,6 +393,9 @@ def run_reference(args) -> None:
         return
     from oracle import reference_path
 
+    # rank 0 is the only rank doing work: give it every host core (torchrun sets
+    # OMP_NUM_THREADS=1 for each rank)
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
     threads = torch.get_num_threads()
     w = make_workload(1234, None)
     runner = reference_path.DecodeLayer(w, HQ, HKV, HEAD_DIM, BLOCK_SIZE)
