@@ -252,11 +252,35 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
   uint8_t* ring = smem + (size_t)warp * S * kStageBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)W * S * kStageBytes) + warp * S;
 
+  // A decode sequence always has at least its own token; an empty history has no softmax.
+  // One warp per KV head writes the zero rows and the flag of every empty history (a range
+  // never starts on one, so no stream unit sees those that sit on range boundaries).
+  auto write_empties = [&]() {
+    for (int base = 0; base < p.num_seqs; base += 32) {
+      const int sq = base + lane;
+      unsigned m = __ballot_sync(0xffffffffu, sq < p.num_seqs && __ldg(p.context_lens + sq) <= 0);
+      while (m) {
+        const int s2 = base + __ffs(m) - 1;
+        m &= m - 1;
+        T* orow = reinterpret_cast<T*>(p.out) + (int64_t)s2 * p.o_tok;
+        for (int e = lane; e < p.group * D; e += 32) {
+          const int qh = e / D, d = e - qh * D;
+          orow[(int64_t)(head * p.group + qh) * p.o_head + d] = from_f32<T>(0.f);
+        }
+        if (lane == 0) set_device_error(p.err, B2P_DEV_LENGTH);
+      }
+    }
+  };
+  const bool empties_warp = blockIdx.x == 0 && warp == W - 1;
+
   Range r;
   const int64_t units_per_cta = W / hpu;
   const int64_t unit = (int64_t)blockIdx.x * units_per_cta + warp / hpu;
   find_range(p, (int64_t)gridDim.x * units_per_cta, unit, r);
-  if (r.begin >= r.end) return;
+  if (r.begin >= r.end) {
+    if (empties_warp) write_empties();
+    return;
+  }
   const int64_t n = r.end - r.begin;
   const int64_t parts = r.parts;
   const int64_t num_slots = p.num_blocks * p.block_size;
@@ -295,6 +319,7 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
     issued = k + 1;
   };
   for (int64_t k = 0; k < S && k < n; ++k) issue(k);
+  if (empties_warp) write_empties();  // while the first tiles are in flight
   if (n > 32) slot_hi = res(p, 32, lane, num_slots);
 
   const int g8 = lane >> 2;  // row group (0..7)
@@ -331,15 +356,7 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
   while (gidx < r.end) {
     const int ctx = __ldg(p.context_lens + seq);
     const int nb = sub_blocks_of(ctx);
-    if (nb == 0) {
-      // A decode sequence always has at least its own token; an empty history has no
-      // softmax. Write zeros and flag it.
-      if (lane == 0) set_device_error(p.err, B2P_DEV_LENGTH);
-      for (int e = lane; e < p.group * D; e += 32) {
-        const int qh = e / D, d = e - qh * D;
-        reinterpret_cast<T*>(p.out)[(int64_t)seq * p.o_tok +
-                                    (int64_t)(head * p.group + qh) * p.o_head + d] = from_f32<T>(0.f);
-      }
+    if (nb == 0) {  // written by the empties warp
       ++seq;
       continue;
     }

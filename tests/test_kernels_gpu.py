@@ -152,11 +152,70 @@ def test_decode_many_short_sequences_cross_cta_merge(ops):
     args = (q.to(dev), kc.to(dev), vc.to(dev), 0, bt.to(dev),
             torch.tensor(ctx, dtype=torch.int32, device=dev), bs, d ** -0.5)
     out1 = ops.paged_decode(*args, workspace=ws).clone()
-    out2 = ops.paged_decode(*args, workspace=ws)
-    assert torch.equal(out1, out2)  # deterministic, and the workspace resets itself
     n_counters = hkv * len(ctx)
+    assert int(ws.view(torch.int32)[:n_counters].abs().sum().item()) == 0  # re-zeroed
+    out2 = ops.paged_decode(*args, workspace=ws)
+    assert torch.equal(out1, out2)  # deterministic
     assert int(ws.view(torch.int32)[:n_counters].abs().sum().item()) == 0
     close(out1, ref.decode_attention(q, kc, vc, 0, tables, ctx, bs, d ** -0.5), torch.bfloat16)
+
+
+def _decode_case(ops, ctx, seed, hq=12, hkv=2, d=128, bs=16, workspace=None, err=None):
+    dev = torch.device("cuda")
+    nb = sum((c + bs - 1) // bs for c in ctx) + 1
+    kc, vc = make_pool(seed, 1, nb, bs, hkv, d, torch.bfloat16)
+    tables, bt = make_tables(seed + 1, ctx, bs, nb)
+    q = torch.randn(len(ctx), hq, d, generator=torch.Generator().manual_seed(seed + 2))
+    q = q.to(torch.bfloat16)
+    out = ops.paged_decode(q.to(dev), kc.to(dev), vc.to(dev), 0, bt.to(dev),
+                           torch.tensor(ctx, dtype=torch.int32, device=dev), bs, d ** -0.5,
+                           workspace=workspace, err_flag=err)
+    return out, ref.decode_attention(q, kc, vc, 0, tables, ctx, bs, d ** -0.5)
+
+
+def test_decode_many_sequences(ops):
+    """1,500 sequences: more sequences than stream units, most ranges hold several."""
+    ctx = np.random.default_rng(61).integers(1, 2500, size=1500).tolist()
+    out, expect = _decode_case(ops, ctx, 60)
+    close(out, expect, torch.bfloat16)
+
+
+def test_decode_one_long_sequence_and_a_long_tail(ops):
+    """A 200k-token history split over every stream unit, and a mix of long and tiny ones."""
+    for ctx in ([200_000], [150_000, 10, 5_000, 60_000, 1, 33_000]):
+        out, expect = _decode_case(ops, ctx, 70)
+        close(out, expect, torch.bfloat16)
+
+
+def test_decode_empty_history_writes_zeros_and_flags(ops):
+    dev = torch.device("cuda")
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ctx = [0, 50, 0, 3000, 17]
+    out, expect = _decode_case(ops, ctx, 80, err=err)
+    assert int(err.item()) & 8  # B2P_DEV_LENGTH
+    assert torch.equal(out[0].float().cpu(), torch.zeros_like(out[0].float().cpu()))
+    assert torch.equal(out[2].float().cpu(), torch.zeros_like(out[2].float().cpu()))
+    keep = [1, 3, 4]
+    close(out[keep], expect[keep], torch.bfloat16)
+
+
+def test_decode_workspace_sizes(ops):
+    """Any workspace the call accepts gives the same results; one too small for the
+    device's stream units is refused with a workspace error before anything runs."""
+    dev = torch.device("cuda")
+    ctx = np.random.default_rng(91).integers(1, 4000, size=400).tolist()
+    full = ops.decode_workspace_size(len(ctx), 12, 2, 128)
+    accepted = 0
+    for shift in range(0, 8):
+        ws = torch.zeros(max(full >> shift, 16), dtype=torch.uint8, device=dev)
+        try:
+            out, expect = _decode_case(ops, ctx, 90, workspace=ws)
+        except ValueError as exc:
+            assert "workspace" in str(exc).lower()
+            continue
+        accepted += 1
+        close(out, expect, torch.bfloat16)
+    assert accepted >= 2
 
 
 def test_decode_garbage_past_context_is_masked(ops):
