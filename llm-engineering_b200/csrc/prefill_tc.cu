@@ -164,6 +164,45 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* m
 
 __device__ __forceinline__ int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
+// Row max of a 64-key S tile (columns 0..31 in r0, 32..63 in r1), four independent
+// chains. kMasked: keys at or past `nvis` are ignored.
+template <bool kMasked>
+__device__ __forceinline__ float row_max64(const uint32_t (&r0)[32], const uint32_t (&r1)[32],
+                                           int nvis) {
+  float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < 32; c += 2) {
+    const float x0 = __uint_as_float(r0[c]), x1 = __uint_as_float(r0[c + 1]);
+    const float x2 = __uint_as_float(r1[c]), x3 = __uint_as_float(r1[c + 1]);
+    a0 = fmaxf(a0, (!kMasked || c < nvis) ? x0 : -INFINITY);
+    a1 = fmaxf(a1, (!kMasked || c + 1 < nvis) ? x1 : -INFINITY);
+    a2 = fmaxf(a2, (!kMasked || 32 + c < nvis) ? x2 : -INFINITY);
+    a3 = fmaxf(a3, (!kMasked || 33 + c < nvis) ? x3 : -INFINITY);
+  }
+  return fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
+}
+
+// P = exp2(S * scale_log2 - m) of a 64-key row, packed in pairs for tcgen05.st; returns
+// the row sum. kMasked: keys at or past `nvis` get 0.
+template <typename T, bool kMasked>
+__device__ __forceinline__ float row_exp64(const uint32_t (&r0)[32], const uint32_t (&r1)[32],
+                                           int nvis, float scale_log2, float m,
+                                           uint32_t (&pk)[32]) {
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {  // tokens 0..31 from r0, 32..63 from r1
+    const float e0 = (!kMasked || 2 * c < nvis) ? fast_exp2(__uint_as_float(r0[2 * c]) * scale_log2 - m) : 0.f;
+    const float e1 = (!kMasked || 2 * c + 1 < nvis) ? fast_exp2(__uint_as_float(r0[2 * c + 1]) * scale_log2 - m) : 0.f;
+    const float e2 = (!kMasked || 32 + 2 * c < nvis) ? fast_exp2(__uint_as_float(r1[2 * c]) * scale_log2 - m) : 0.f;
+    const float e3 = (!kMasked || 33 + 2 * c < nvis) ? fast_exp2(__uint_as_float(r1[2 * c + 1]) * scale_log2 - m) : 0.f;
+    s0 += e0 + e1;
+    s1 += e2 + e3;
+    pk[c] = pack2<T>(e0, e1);
+    pk[16 + c] = pack2<T>(e2, e3);
+  }
+  return s0 + s1;
+}
+
 // Work item k -> (sequence, query tile), tiles of a sequence enumerated last first (the
 // last tiles see the most keys, so they start early). One warp; all lanes return it.
 __device__ bool find_item(const PrefillParams& p, int k, int& seq, int& tile) {
@@ -408,14 +447,11 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
       tmem_ld32(s_col + 32, r1);
       tmem_wait_ld();
       const int key0 = j * kN;
-      // key c of this tile is visible iff key0 + c <= pos (then also < ctx)
+      // key c of this tile is visible iff key0 + c <= pos (then also < ctx). Tiles that
+      // every row of the warp sees whole (all but the diagonal ones) skip the masks.
       const int nvis = valid_row ? min(kN, pos - key0 + 1) : 0;
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        if (c < nvis) mx = fmaxf(mx, __uint_as_float(r0[c]));
-        if (32 + c < nvis) mx = fmaxf(mx, __uint_as_float(r1[c]));
-      }
+      const bool whole = __all_sync(0xffffffffu, nvis == kN);
+      float mx = whole ? row_max64<false>(r0, r1, nvis) : row_max64<true>(r0, r1, nvis);
       mx = mx * p.scale_log2;  // scale_log2 > 0 keeps the arg-max
       bool rescale = false;
       float alpha = 1.f;
@@ -446,17 +482,8 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
         l *= alpha;
       }
       uint32_t pk[32];
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {  // tokens 0..31 from r0, 32..63 from r1
-        const float e0 = 2 * c < nvis ? fast_exp2(__uint_as_float(r0[2 * c]) * p.scale_log2 - m) : 0.f;
-        const float e1 = 2 * c + 1 < nvis ? fast_exp2(__uint_as_float(r0[2 * c + 1]) * p.scale_log2 - m) : 0.f;
-        const float e2 = 32 + 2 * c < nvis ? fast_exp2(__uint_as_float(r1[2 * c]) * p.scale_log2 - m) : 0.f;
-        const float e3 = 33 + 2 * c < nvis ? fast_exp2(__uint_as_float(r1[2 * c + 1]) * p.scale_log2 - m) : 0.f;
-        rs += (e0 + e1) + (e2 + e3);
-        pk[c] = pack2<T>(e0, e1);
-        pk[16 + c] = pack2<T>(e2, e3);
-      }
+      const float rs = whole ? row_exp64<T, false>(r0, r1, nvis, p.scale_log2, m, pk)
+                             : row_exp64<T, true>(r0, r1, nvis, p.scale_log2, m, pk);
       l += rs;
       tmem_st32(s_col, pk);
       tmem_wait_st();
