@@ -29,6 +29,10 @@ rate is scaled to 28 layers. When the requested warm-up + timed steps would take
 REFERENCE_BUDGET_S of CPU time, each step serves a prefix of the batch instead, and the
 line says how many sequences.
 
+``--workload prefill`` measures packed causal prefill + KV write instead: 32 prompts with
+lengths log-uniform in [64, 8192] (49,659 tokens), one layer; value = prompt tokens/s,
+roofline = K3's causal FLOPs / its CUDA-event time against the measured bf16 peak.
+
 Multi-GPU: one process per GPU (torchrun); every rank runs an independent replica of the
 workload (weak scaling, no collective on the data path); timing is the max over ranks.
 """
@@ -487,15 +491,23 @@ def make_prefill_workload(seed: int, device: torch.device):
 
 def run_prefill(args) -> None:
     """Packed prefill + KV write (one layer): K1 scatters every prompt token's K/V into the
-    pool, K3 runs causal attention over the packed prompts reading K/V from the pool."""
+    pool, K3 runs causal attention over the packed prompts reading K/V from the pool. Under
+    torchrun every rank runs an independent replica (its own seeded prompts and pool)."""
+    import datetime
+
     import __graft_entry__ as entry
 
     entry.load_package()
     from llm_engineering_b200 import ops
 
-    dev = torch.device("cuda", 0)
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    w = make_prefill_workload(4321, dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    w = make_prefill_workload(4321, dev)  # every replica serves the same prompts
     slots = torch.from_numpy(w["slots"]).to(dev)
     tables = torch.from_numpy(w["tables"]).to(dev)
     cu = torch.from_numpy(w["cu"]).to(dev)
@@ -506,18 +518,26 @@ def run_prefill(args) -> None:
     stream = torch.cuda.current_stream(dev)
     max_q = int(w["lens"].max())
 
-    def step(evs=None):
-        ops.kv_write(w["kc"], w["vc"], 0, slots, w["k"], w["v"], err)
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def step(evs=None, bufs=None):
+        q, k, v, sl, tb, c, cl = bufs or (w["q"], w["k"], w["v"], slots, tables, cu, ctx)
+        ops.kv_write(w["kc"], w["vc"], 0, sl, k, v, err)
         if evs:
             evs[0].record(stream)
-        ops.paged_prefill(w["q"], w["kc"], w["vc"], 0, tables, cu, ctx, max_q, BLOCK_SIZE, scale,
+        ops.paged_prefill(q, w["kc"], w["vc"], 0, tb, c, cl, max_q, BLOCK_SIZE, scale,
                           out=out, err_flag=err)
         if evs:
             evs[1].record(stream)
 
     for _ in range(args.warmup):
         step()
-    torch.cuda.synchronize(dev)
+    barrier()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -527,36 +547,195 @@ def run_prefill(args) -> None:
             step(evs[i])
         t1.record(stream)
         torch.cuda.synchronize(dev)
+    barrier()
     if int(err.item()) != 0:
         raise RuntimeError(f"device error flag set: {int(err.item())}")
     ms = t0.elapsed_time(t1) / args.steps
     k3_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
-    lens = w["lens"].astype(np.float64)
-    flops = 4.0 * HQ * HEAD_DIM * float((lens * (lens + 1) / 2).sum())
-    tokens = float(lens.sum())
-    peaks_path = REPO / "MEASURED_PEAKS.json"
-    peaks = json.loads(peaks_path.read_text()) if peaks_path.exists() else {}
-    peak = float(peaks.get("bf16_tflops", 1590.0))
-    achieved = flops / (k3_ms / 1e3) / 1e12
+
+    # ---- e2e: the same step through the public ops API from pinned HOST buffers (prompt
+    # Q/K/V, slot mapping, block tables, cu_seqlens, lengths in; attention output out)
+    host = [t.cpu().pin_memory() for t in (w["q"], w["k"], w["v"])]
+    host += [torch.from_numpy(a).pin_memory()
+             for a in (w["slots"], w["tables"], w["cu"], w["lens"].astype(np.int32))]
+    h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    d2h = h_out.numel() * h_out.element_size()
+
+    def e2e_step():
+        step(bufs=tuple(t.to(dev, non_blocking=True) for t in host))
+        h_out.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+
+    times = torch.tensor([ms, k3_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms, k3_ms, e2e_ms = times.tolist()
+    if rank == 0:
+        lens = w["lens"].astype(np.float64)
+        flops = 4.0 * HQ * HEAD_DIM * float((lens * (lens + 1) / 2).sum())
+        tokens = float(lens.sum())
+        peaks_path = REPO / "MEASURED_PEAKS.json"
+        peaks = json.loads(peaks_path.read_text()) if peaks_path.exists() else {}
+        peak = float(peaks.get("bf16_tflops", 1590.0))
+        achieved = flops / (k3_ms / 1e3) / 1e12
+        line = {
+            "metric": "prefill tok/s (packed causal prefill + KV write, Qwen2.5-1.5B layer shape)",
+            "value": round(tokens * world / (ms / 1e3), 1), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) Q/K/V, 32 prompts log-uniform [64, 8192])",
+            "config": {"workload": "packed prefill + KV write, 1 layer, 32 prompts, 12/2 heads, "
+                                   "head_dim 128, block 16, fragmented 16384-block pool",
+                       "total_tokens": int(tokens), "max_prompt": max_q,
+                       "l2": "inputs larger than L2 (152 MB of Q per step)",
+                       "parallelism": f"dp{world} (independent replicas)"},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                         "peak_source": "measured bf16_tflops (burst)" if peaks else "fallback",
+                         "traffic": None, "causal_flops": flops, "kernel": "paged_prefill_tc",
+                         "kernel_us": round(k3_ms * 1e3, 2)},
+            "kv_write_us": round((ms - k3_ms) * 1e3, 2),
+            "e2e": {"value": round(tokens * world / (e2e_ms / 1e3), 1), "unit": "tok/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_prefill_baseline(w)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_prefill_baseline(w) -> dict:
+    """The oracle's prefill restatement (KV scatter + per-prompt gather + fp32 causal
+    attention) on the host cores, over the workload's prompts in order until ~20,000 tokens,
+    as tokens per second."""
+    from oracle import paged as ref
+
+    threads = torch.get_num_threads()
+    lens = w["lens"].astype(np.int64)
+    n = 1
+    while n < len(lens) and lens[:n + 1].sum() <= 20000:
+        n += 1
+    rows = int(lens[:n].sum())
+    q = w["q"][:rows].cpu()
+    k, v = w["k"][:rows].cpu(), w["v"][:rows].cpu()
+    kc = torch.zeros(1, PREFILL_POOL_BLOCKS * BLOCK_SIZE, HKV, HEAD_DIM, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    tables = [row[row >= 0].tolist() for row in w["tables"][:n]]
+    cu = w["cu"][:n + 1].tolist()
+    t = time.perf_counter()
+    ref.scatter(kc, vc, 0, w["slots"][:rows].tolist(), k, v)
+    ref.prefill_attention(q, kc, vc, 0, tables, cu, lens[:n].tolist(), BLOCK_SIZE,
+                          HEAD_DIM ** -0.5)
+    dt = time.perf_counter() - t
+    return {"value": round(rows / dt, 1), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"the first {n} prompts ({rows} tokens): scatter + per-prompt gather + "
+                      "fp32 causal attention, one layer"}
+
+
+def run_metadata(args) -> None:
+    """K4 alone on a mixed continuous-batching step: 192 decode sequences (contexts
+    U[256, 2048]) plus 4 chunked-prefill slices of 512 tokens (512..2048 tokens of history
+    each), block tables read from a device-resident mirror of the block pool's tables."""
+    import __graft_entry__ as entry
+
+    entry.load_package()
+    from llm_engineering_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    rng = np.random.default_rng(77)
+    n_dec, n_pre, slice_len = 192, 4, 512
+    dec_ctx = rng.integers(256, 2049, size=n_dec)
+    pre_ctx = rng.integers(1, 4, size=n_pre) * slice_len + slice_len  # chunk 2..4 of a prompt
+    ctx = np.concatenate([dec_ctx, pre_ctx]).astype(np.int32)
+    qlen = np.concatenate([np.ones(n_dec), np.full(n_pre, slice_len)]).astype(np.int32)
+    width = int(((ctx + BLOCK_SIZE - 1) // BLOCK_SIZE).max())
+    perm = rng.permutation(POOL_BLOCKS).astype(np.int32)
+    mirror = np.full((len(ctx) + 16, width), -1, dtype=np.int32)
+    rows = rng.permutation(len(ctx) + 16)[:len(ctx)].astype(np.int32)  # engine row of each
+    used = 0
+    for i, c in enumerate(ctx):
+        nb = (int(c) + BLOCK_SIZE - 1) // BLOCK_SIZE
+        mirror[rows[i], :nb] = perm[used:used + nb]
+        used += nb
+    total_q = int(qlen.sum())
+    d_q, d_ctx = torch.from_numpy(qlen).to(dev), torch.from_numpy(ctx).to(dev)
+    d_rows, d_mirror = torch.from_numpy(rows).to(dev), torch.from_numpy(mirror).to(dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return ops.build_metadata(d_q, d_ctx, d_rows, d_mirror, BLOCK_SIZE, total_q, width, err)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    # The Python call (six output allocations + the C call) takes longer than the kernel, so
+    # launches are captured in a CUDA graph (10 back to back) and replayed: the events then
+    # time device work only.
+    per_graph = 10
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        step()  # warm the capture stream's allocator pool
+        torch.cuda.synchronize(dev)
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(per_graph):
+                md = step()
+    stream.wait_stream(side)
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    with ClockSampler(dev) as clocks:
+        for a, b in evs:
+            a.record(stream)
+            graph.replay()
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+    if int(err.item()) != 0:
+        raise RuntimeError(f"device error flag set: {int(err.item())}")
+    us = statistics.median(a.elapsed_time(b) for a, b in evs) * 1e3 / per_graph
+    out_bytes = sum(t.numel() * t.element_size() for t in md.values())
+    in_bytes = 4 * (3 * len(ctx)) + 4 * len(ctx) * width
     line = {
-        "metric": "prefill tok/s (packed causal prefill + KV write, Qwen2.5-1.5B layer shape)",
-        "value": round(tokens / (ms / 1e3), 1), "unit": "tok/s", "n_gpus": 1,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-        "higher_is_better": True, "dtype": "bf16",
-        "data": "synthetic (seeded N(0,1) Q/K/V, 32 prompts log-uniform [64, 8192])",
-        "config": {"workload": "packed prefill + KV write, 1 layer, 32 prompts, 12/2 heads, "
-                               "head_dim 128, block 16, fragmented 16384-block pool",
-                   "total_tokens": int(tokens), "max_prompt": max_q},
-        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
-                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-                     "peak_source": "measured bf16_tflops (burst)" if peaks else "fallback",
-                     "causal_flops": flops, "kernel": "paged_prefill_tc",
-                     "kernel_us": round(k3_ms * 1e3, 2)},
-        "kv_write_us": round((ms - k3_ms) * 1e3, 2),
-        "gpu_launches": 2 * args.steps,
+        "metric": "batch metadata build time per mixed step (cu_seqlens, positions, slot "
+                  "mapping, logit rows, padded block tables)",
+        "value": round(us, 2), "unit": "us", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": False, "dtype": "int32/int64",
+        "data": "synthetic (seeded contexts and block ids)",
+        "config": {"workload": "192 decode seqs ctx U[256,2048] + 4 chunked-prefill slices of "
+                               "512 tokens, block 16, rows from a 212-row table mirror",
+                   "total_q": total_q, "table_width": width},
+        "roofline": {"bound": "launch latency", "bytes_per_launch": in_bytes + out_bytes,
+                     "kernel": "build_metadata", "kernel_us": round(us, 2)},
+        "gpu_launches": args.steps * per_graph,
+        "timing": "CUDA graph of 10 back-to-back launches, replayed; value = replay time / 10",
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)
+    del graph
 
 
 def main() -> None:
@@ -566,9 +745,10 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "metadata"], default="decode",
                     help="decode (default): the headline decode-attention metric; prefill: "
-                         "packed prefill + KV write of 32 prompts")
+                         "packed prefill + KV write of 32 prompts; metadata: K4 on a mixed "
+                         "decode + chunked-prefill step")
     ap.add_argument("--layers", type=int, default=NUM_LAYERS,
                     help="layers of the decode pool (28 for the metric; fewer for profiling)")
     args = ap.parse_args()
@@ -576,6 +756,8 @@ def main() -> None:
         args.warmup = 3
     if args.workload == "prefill":
         run_prefill(args)
+    elif args.workload == "metadata":
+        run_metadata(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
