@@ -269,6 +269,52 @@ def test_decode_full_benchmark_workload(ops):
     close(out, expect, torch.bfloat16)
 
 
+def churned_tables(rng, ctx, bs, num_blocks, churn=0.3):
+    """Block tables after allocation churn: blocks are handed out from a FIFO free list,
+    30% of them are freed in random order and handed out again, so every table mixes
+    runs of old and recycled blocks (as after preemption and completion in the engine)."""
+    need = [(c + bs - 1) // bs for c in ctx]
+    free = list(range(num_blocks))
+    tables = [[] for _ in ctx]
+    # interleaved first allocation (sequences grow together under continuous batching)
+    pending = list(range(len(ctx)))
+    while pending:
+        for i in list(pending):
+            tables[i].append(free.pop(0))
+            if len(tables[i]) == need[i]:
+                pending.remove(i)
+    # free 30% of all allocated blocks in random order, then reallocate them at the
+    # positions they were taken from (FIFO order of the free list)
+    taken = [(i, j) for i, t in enumerate(tables) for j in range(len(t))]
+    victims = [taken[k] for k in rng.permutation(len(taken))[: int(churn * len(taken))]]
+    for i, j in victims:
+        free.append(tables[i][j])
+        tables[i][j] = None
+    for i, j in victims:
+        tables[i][j] = free.pop(0)
+    width = max(len(t) for t in tables)
+    bt = np.full((len(ctx), width), -1, dtype=np.int32)
+    for i, t in enumerate(tables):
+        bt[i, :len(t)] = t
+    return tables, torch.from_numpy(bt)
+
+
+def test_decode_long_context_churned_tables_7b_shape(ops):
+    """Qwen2.5-7B attention shape (28 Q / 4 KV heads, group 7), 16 sequences with contexts
+    U[8192, 32768], block tables fragmented by allocation churn."""
+    dev = torch.device("cuda")
+    hq, hkv, d, bs = 28, 4, 128, 16
+    rng = np.random.default_rng(97)
+    ctx = rng.integers(8192, 32769, size=16).tolist()
+    nb = sum((c + bs - 1) // bs for c in ctx) + 64
+    tables, bt = churned_tables(rng, ctx, bs, nb)
+    kc, vc = make_pool(98, 1, nb, bs, hkv, d, torch.bfloat16)
+    q = torch.randn(len(ctx), hq, d, generator=torch.Generator().manual_seed(99)).to(torch.bfloat16)
+    out = ops.paged_decode(q.to(dev), kc.to(dev), vc.to(dev), 0, bt.to(dev),
+                           torch.tensor(ctx, dtype=torch.int32, device=dev), bs, d ** -0.5)
+    close(out, ref.decode_attention(q, kc, vc, 0, tables, ctx, bs, d ** -0.5), torch.bfloat16)
+
+
 # ------------------------------------------------------------------ K3 prefill
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("shape", [(12, 2, 128, 16), (14, 2, 64, 16), (28, 4, 128, 32)])

@@ -124,3 +124,69 @@ def test_bf16_runner_logits_match_reference_path():
     assert runner.device_error() == 0
     assert both.checked > 6
     assert both.max_err < 5e-2, both.max_err
+
+
+def test_chunked_prefill_slices_in_a_mixed_step_match_whole_prefill():
+    """A 700-token prompt prefilled as two slices (300, then 400 tokens that attend to the
+    first 300 through the pool), the second slice sharing its step with 12 decodes, gives
+    the same last-token logits as one whole-prompt prefill; the decodes match the
+    reference-style packed runner (fp32) in the same step."""
+    dev = torch.device("cuda")
+    base = small_1p5b_attention_model(seed=3)
+    ours_model = copy.deepcopy(base).to(dev, torch.bfloat16)
+    bs, blocks = 16, 512
+    rng = np.random.default_rng(21)
+    prompt = tuple(int(x) for x in rng.integers(0, 1000, size=700))
+    whole_blocks = tuple(range(100, 100 + 44))  # 44 blocks of 16 cover 700 tokens
+
+    # whole-prompt prefill on its own pool
+    st_a = PagedKVStorage(2, blocks, bs, 2, 128, torch.bfloat16, dev)
+    run_a = B200PagedModelRunner(copy.deepcopy(ours_model), dev, st_a)
+    seq_full = eng.SequenceState(eng.Request("p", prompt, 8))
+    whole = run_a.forward([eng.ModelExecution(seq_full, eng.ExecutionPhase.PREFILL,
+                                              block_ids=whole_blocks, block_size=bs)])
+
+    # the same prompt in two slices on a second pool; step 2 also carries 12 decodes
+    st_b = PagedKVStorage(2, blocks, bs, 2, 128, torch.bfloat16, dev)
+    run_b = B200PagedModelRunner(ours_model, dev, st_b)
+    seq_part = eng.SequenceState(eng.Request("p", prompt[:300], 8))
+    run_b.forward([eng.ModelExecution(seq_part, eng.ExecutionPhase.PREFILL,
+                                      block_ids=whole_blocks[:19], block_size=bs)])
+    # decodes: prefill their prompts first (one step), then one decode token each
+    dec = []
+    for i in range(12):
+        n = int(rng.integers(20, 200))
+        toks = tuple(int(x) for x in rng.integers(0, 1000, size=n))
+        blk = tuple(range(200 + i * 16, 200 + i * 16 + (n + 1 + bs - 1) // bs))
+        dec.append((eng.SequenceState(eng.Request(f"d{i}", toks, 8)), blk))
+    run_b.forward([eng.ModelExecution(s, eng.ExecutionPhase.PREFILL, block_ids=b, block_size=bs)
+                   for s, b in dec])
+    for s, _ in dec:
+        s.append_token(7)
+    step = [eng.ModelExecution(s, eng.ExecutionPhase.DECODE, block_ids=b, block_size=bs)
+            for s, b in dec]
+    step.append(eng.ModelExecution(seq_full, eng.ExecutionPhase.PREFILL, block_ids=whole_blocks,
+                                   block_size=bs, query_length=400))
+    got = run_b.forward(step).float().cpu()
+    assert run_b.device_error() == 0 and run_a.device_error() == 0
+    # the chunked prefill's last token == whole prefill's last token (bf16 path both times)
+    w0 = whole[0].float().cpu()
+    assert (got[-1] - w0).abs().max().item() < 5e-2
+    top2 = torch.topk(w0, 2).values
+    if (top2[0] - top2[1]).item() > 5e-2:  # a confident top-1 must agree
+        assert got[-1].argmax().item() == w0.argmax().item()
+
+    # the decode rows against the reference-style path in fp32 on the same weights
+    ref_model = copy.deepcopy(base).float()
+    kr = torch.zeros(2, blocks * bs, 2, 128)
+    vr = torch.zeros(2, blocks * bs, 2, 128)
+    reference = ReferencePackedRunner(ref_model, kr, vr, bs)
+    for s, _ in dec:  # rebuild their history in the reference pool: prompt, then decode
+        s.generated_token_ids.clear()
+    reference.forward([eng.ModelExecution(s, eng.ExecutionPhase.PREFILL, block_ids=b,
+                                          block_size=bs) for s, b in dec])
+    for s, _ in dec:
+        s.append_token(7)
+    want = reference.forward([eng.ModelExecution(s, eng.ExecutionPhase.DECODE, block_ids=b,
+                                                 block_size=bs) for s, b in dec])
+    assert (got[:12] - want).abs().max().item() < 5e-2
