@@ -4,10 +4,11 @@ Workload (default): the Qwen2.5-1.5B decode-attention layer shape — 256 sequen
 context lengths uniform in [512, 4096], 12 query / 2 KV heads, head_dim 128, block size
 16, block tables drawn as a seeded random permutation of a 65,536-block pool, Q/K/V drawn
 N(0,1), bf16, one query token per sequence. One step = the attention half of one decode
-step of the 28-layer model: for each of 28 layers of the pool, K1 writes each sequence's
-newest K/V row into its slot and K2 attends over the paged history (the pool's physical
-slots are shared by all layers, as in the reference storage). Each K2 launch reads
-~0.6 GB of K/V, more than the 126 MB L2, so no flush is needed between launches.
+step of the 28-layer model: for each of 28 layers of the pool, one fused launch (K1 + K2,
+``b2p_paged_decode_append``) stores each sequence's newest K/V row at its slot and attends
+over the paged history (the pool's physical slots are shared by all layers, as in the
+reference storage). Each launch reads ~0.6 GB of K/V, more than the 126 MB L2, so no flush
+is needed between launches.
 
 ``value``  decode tokens/s (a token = one sequence's query through all 28 attention
            layers), whole job, inputs resident in HBM, device time (CUDA events, max over
@@ -15,10 +16,10 @@ slots are shared by all layers, as in the reference storage). Each K2 launch rea
 ``e2e``    the same metric through the public ops API with pinned HOST buffers: each step
            copies q, the new K/V rows, block tables and context lengths host->device and
            the attention output device->host inside the timed region.
-``roofline`` HBM bytes the K2 kernel must move per launch (1,024 B x sum(ctx) of K+V, plus
-           Q/O and block tables) / its average launch time (CUDA events around every K2
-           launch of the timed region), against the measured copy bandwidth in
-           MEASURED_PEAKS.json.
+``roofline`` HBM bytes the decode kernel must move per launch (1,024 B x sum(ctx) of K+V,
+           plus Q/O, the new K/V rows read and stored, and block tables) / its average
+           launch time (CUDA events around every launch of the timed region), against the
+           measured copy bandwidth in MEASURED_PEAKS.json.
 ``clocks`` SM clock and throttle reasons sampled through NVML every 10 ms during the
            timed region.
 
@@ -187,8 +188,9 @@ def make_workload(seed: int, device: torch.device | None, layers: int = 1):
 def algorithmic_bytes(ctx: np.ndarray) -> float:
     kv = 2 * HKV * HEAD_DIM * 2 * float(ctx.sum())          # K + V rows read
     qo = 2 * NUM_SEQS * HQ * HEAD_DIM * 2                   # Q read + O written
+    new = 4 * NUM_SEQS * HKV * HEAD_DIM * 2                 # new K/V rows read + stored
     bt = 4 * float(((ctx + BLOCK_SIZE - 1) // BLOCK_SIZE).sum())
-    return kv + qo + bt + 4 * NUM_SEQS
+    return kv + qo + new + bt + 4 * NUM_SEQS
 
 
 def dist_setup():
@@ -222,7 +224,6 @@ def run_ours(args) -> None:
     kc, vc = w["kc"], w["vc"]
     q = w["q"].to(dev)
     new_k, new_v = w["new_k"].to(dev), w["new_v"].to(dev)
-    slots = torch.from_numpy(w["slots"]).to(dev)
     tables = torch.from_numpy(w["tables"]).to(dev)
     ctx = torch.from_numpy(w["ctx"]).to(dev)
     out = torch.empty_like(q)
@@ -230,15 +231,15 @@ def run_ours(args) -> None:
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     scale = HEAD_DIM ** -0.5
     stream = torch.cuda.current_stream(dev)
-    launches_per_step = 2 * L
+    launches_per_step = L
 
     def step(events=None):
         for layer in range(L):
-            ops.kv_write(kc, vc, layer, slots, new_k[layer], new_v[layer], err)
             if events is not None:
                 events[layer][0].record(stream)
-            ops.paged_decode(q[layer], kc, vc, layer, tables, ctx, BLOCK_SIZE, scale,
-                             out=out[layer], workspace=ws, err_flag=err)
+            ops.paged_decode_append(q[layer], new_k[layer], new_v[layer], kc, vc, layer, tables,
+                                    ctx, BLOCK_SIZE, scale, out=out[layer], workspace=ws,
+                                    err_flag=err)
             if events is not None:
                 events[layer][1].record(stream)
 
@@ -271,24 +272,22 @@ def run_ours(args) -> None:
     h_q = w["q"].cpu().pin_memory()
     h_k = w["new_k"].cpu().pin_memory()
     h_v = w["new_v"].cpu().pin_memory()
-    h_slots = torch.from_numpy(w["slots"]).pin_memory()
     h_tables = torch.from_numpy(w["tables"]).pin_memory()
     h_ctx = torch.from_numpy(w["ctx"]).pin_memory()
     h_out = torch.empty(q.shape, dtype=q.dtype).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_slots, h_tables, h_ctx))
+    h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_tables, h_ctx))
     d2h = h_out.numel() * h_out.element_size()
 
     def e2e_step():
-        ds = h_slots.to(dev, non_blocking=True)
         dt = h_tables.to(dev, non_blocking=True)
         dc = h_ctx.to(dev, non_blocking=True)
         dq = h_q.to(dev, non_blocking=True)
         dk = h_k.to(dev, non_blocking=True)
         dv = h_v.to(dev, non_blocking=True)
         for layer in range(L):
-            ops.kv_write(kc, vc, layer, ds, dk[layer], dv[layer], err)
-            ops.paged_decode(dq[layer], kc, vc, layer, dt, dc, BLOCK_SIZE, scale,
-                             out=out[layer], workspace=ws, err_flag=err)
+            ops.paged_decode_append(dq[layer], dk[layer], dv[layer], kc, vc, layer, dt, dc,
+                                    BLOCK_SIZE, scale, out=out[layer], workspace=ws,
+                                    err_flag=err)
         h_out.copy_(out, non_blocking=True)
 
     for _ in range(args.warmup):
@@ -346,7 +345,7 @@ def run_ours(args) -> None:
                 "frac_of_8000": round(achieved / 8000.0, 4),
                 "traffic": K2_TRAFFIC_BYTES,
                 "algorithmic_bytes": alg,
-                "kernel": "paged_decode_tc",
+                "kernel": "paged_decode_tc (fused KV write)",
                 "kernel_us": round(k2_ms * 1e3, 2),
             },
             "e2e": {

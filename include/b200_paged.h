@@ -146,6 +146,32 @@ B2P_API int b2p_paged_decode_noalloc(const void* q, int64_t q_tok_stride, int64_
                                      int dtype, int32_t* err_flag, void* stream);
 
 /*
+ * K1 and K2 for the decode rows of a step in one launch: each sequence's newest K/V row
+ * (the key at position context_lens[i] - 1) is stored into the pool at the slot its block
+ * table gives for that position, and the sequence's query attends over its whole history,
+ * that row included. Same result as b2p_kv_write over the step's decode rows with
+ * slot_mapping[i] = block_tables[i][(ctx_i - 1) / block_size] * block_size
+ * + (ctx_i - 1) % block_size (the decode write of PagedKVCache.update_and_gather,
+ * serving/engine/paged_kv_cache.py:51-58) followed by b2p_paged_decode, without the second
+ * launch or a second pass over the new rows.
+ *   new_keys, new_values : [num_seqs, num_kv_heads, head_dim] (strides in elements); rows
+ *                          16-byte aligned
+ * All other arguments, the workspace and the results are those of b2p_paged_decode.
+ */
+B2P_API int b2p_paged_decode_append(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
+                                    const void* new_keys, int64_t k_tok_stride,
+                                    int64_t k_head_stride, const void* new_values,
+                                    int64_t v_tok_stride, int64_t v_head_stride, void* key_cache,
+                                    void* value_cache, int64_t layer_index, int64_t num_layers,
+                                    int64_t num_slots, const int32_t* block_tables,
+                                    int64_t block_table_stride, const int32_t* context_lens,
+                                    int num_seqs, int num_q_heads, int num_kv_heads, int head_dim,
+                                    int block_size, float scale, void* out, int64_t out_tok_stride,
+                                    int64_t out_head_stride, void* workspace,
+                                    size_t workspace_bytes, int dtype, int32_t* err_flag,
+                                    void* stream);
+
+/*
  * K3 — packed variable-length causal attention (prefill and chunked prefill) over the
  * paged pool. Replaces, for PREFILL executions, the same reference steps as K2 plus the
  * causal tril blocks of build_attention_mask (serving/engine/attention_mask.py:37-45).

@@ -37,6 +37,7 @@ EXPORTED_SYMBOLS = (
     "b2p_paged_decode_workspace_size",
     "b2p_paged_decode",
     "b2p_paged_decode_noalloc",
+    "b2p_paged_decode_append",
     "b2p_paged_prefill",
     "b2p_build_metadata",
 )
@@ -69,6 +70,11 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _i32,
         [_p, _i64, _i64, _p, _p, _i64, _i64, _i64, _p, _i64, _p, _i32, _i32, _i32, _i32, _i32,
          _f32, _p, _i64, _i64, _i32, _p, _p],
+    ),
+    "b2p_paged_decode_append": (
+        _i32,
+        [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _p, _i64, _i64, _i64, _p, _i64, _p,
+         _i32, _i32, _i32, _i32, _i32, _f32, _p, _i64, _i64, _p, _sz, _i32, _p, _p],
     ),
     "b2p_paged_prefill": (
         _i32,

@@ -57,6 +57,17 @@ struct DecodeParams {
   float* partials;   // [num_kv_heads][units][2][record]
   int32_t* counters; // [num_kv_heads][num_seqs], zero between launches
   int32_t* err;
+  // Append mode (new_k != nullptr): each sequence's newest K/V row (the key at position
+  // ctx - 1) comes in here; the warp that streams the sequence's last sub-block puts it
+  // into its shared-memory tile and stores it into the pool at the slot the block table
+  // gives for that position (what a KV write with the step's slot mapping would do).
+  const uint8_t* new_k;
+  int64_t nk_tok, nk_head;  // element strides
+  const uint8_t* new_v;
+  int64_t nv_tok, nv_head;
+  uint8_t* kpool;
+  uint8_t* vpool;
+  int num_kv_heads;
 };
 
 template <int D, int NT>
@@ -251,6 +262,9 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
   const int head = blockIdx.y * hpu + warp % hpu;  // KV head
   uint8_t* ring = smem + (size_t)warp * S * kStageBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)W * S * kStageBytes) + warp * S;
+  // slot of each stage's first row (append mode stores the new row relative to it)
+  int32_t* stage_slot =
+      reinterpret_cast<int32_t*>(smem + (size_t)W * S * kStageBytes + W * S * 8) + warp * S;
 
   // A decode sequence always has at least its own token; an empty history has no softmax.
   // One warp per KV head writes the zero rows and the flag of every empty history (a range
@@ -312,6 +326,7 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
       const int stage = (int)(k % S);
       uint8_t* kdst = ring + stage * kStageBytes;
       const int c3 = (int)(slot < 0 ? num_slots : slot);
+      stage_slot[stage] = c3;
       mbar_arrive_expect_tx(&full[stage], kStageBytes);
       tma_load_5d(kdst, &kmap, &full[stage], 0, 0, head, c3, p.layer);
       tma_load_5d(kdst + kTileBytes, &vmap, &full[stage], 0, 0, head, c3, p.layer);
@@ -363,6 +378,17 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
     const int lb0 = (int)(gidx - cb);
     const int64_t seg_end = min(r.end, cb + nb);
     const int lb1 = (int)(seg_end - cb);
+
+    // Append mode: warm L1 with this sequence's new K/V rows if its last sub-block is in
+    // the segment (they are put into that tile when it arrives).
+    const bool appends = p.new_k != nullptr && lb1 == nb;
+    if (appends && lane < 2 * (D * (int)sizeof(T) / 128)) {
+      const int lines = D * (int)sizeof(T) / 128;
+      const bool isv = lane >= lines;
+      const uint8_t* row = isv ? p.new_v + ((int64_t)seq * p.nv_tok + (int64_t)head * p.nv_head) * sizeof(T)
+                               : p.new_k + ((int64_t)seq * p.nk_tok + (int64_t)head * p.nk_head) * sizeof(T);
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(row + (isv ? lane - lines : lane) * 128));
+    }
 
     // Warm L1 with the next sequence's query rows (read when its segment starts).
     if (seg_end < r.end && lb1 == nb && seq + 1 < p.num_seqs) {
@@ -417,6 +443,32 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
         const int zero_bytes = (kSub - valid) * D * 2;
         uint4* z = reinterpret_cast<uint4*>(vtile + valid * D * 2);
         for (int i = lane; i < zero_bytes / 16; i += 32) z[i] = make_uint4(0, 0, 0, 0);
+        __syncwarp();
+      }
+      const bool patched = appends && lb == nb - 1;
+      if (patched) {
+        // The newest token (row valid - 1 of this tile): its K and V rows replace what the
+        // pool held at its slot, in the tile (16-byte chunks at their swizzled places) and
+        // in the pool. No other stream unit reads that slot in this launch.
+        const int rrow = valid - 1;
+        const int32_t slot = stage_slot[stage] + rrow;
+        const bool in_pool = stage_slot[stage] < (int32_t)num_slots;
+        constexpr int kChunks = D * 2 / 16;  // 16-byte chunks per row
+        for (int c = lane; c < 2 * kChunks; c += 32) {
+          const bool isv = c >= kChunks;
+          const int cc = isv ? c - kChunks : c;
+          const uint4 val = __ldg(reinterpret_cast<const uint4*>(
+                                isv ? p.new_v + ((int64_t)seq * p.nv_tok + (int64_t)head * p.nv_head) * 2
+                                    : p.new_k + ((int64_t)seq * p.nk_tok + (int64_t)head * p.nk_head) * 2) + cc);
+          const int d = cc * 8;
+          const uint32_t off = (uint32_t)((rrow * (D / 64) + d / 64) * 128 + (d % 64) * 2);
+          *reinterpret_cast<uint4*>((isv ? vtile : ktile) + swz128(off)) = val;
+          if (in_pool) {
+            uint8_t* pool = isv ? p.vpool : p.kpool;
+            const int64_t e = (((int64_t)p.layer * num_slots + slot) * p.num_kv_heads + head) * D + d;
+            *reinterpret_cast<uint4*>(pool + e * 2) = val;
+          }
+        }
         __syncwarp();
       }
       const uint32_t kbase = smem_u32(ktile);
@@ -503,7 +555,7 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
       // Refill this stage with the item S ahead. All reads of the stage are complete (their
       // results fed the MMAs above); generic writes (the zeroed rows) need a proxy fence
       // before the TMA unit writes the same bytes.
-      if (valid < kSub) fence_proxy_async_smem();
+      if (valid < kSub || patched) fence_proxy_async_smem();
       __syncwarp();
       if (k + S < n) issue(k + S);
     }
@@ -676,8 +728,9 @@ template <typename T, int D, int NT, int S, int W>
 Plan make_plan() {
   Plan pl;
   pl.fn = reinterpret_cast<const void*>(&paged_decode_tc<T, D, NT, S, W>);
-  // W rings of S stages (K and V tile each), W*S mbarriers, + slack for the 1024 alignment.
-  pl.smem = W * S * (2 * kSub * D * 2) + W * S * 8 + 1024;
+  // W rings of S stages (K and V tile each), W*S mbarriers, W*S stage slots, + slack for
+  // the 1024 alignment.
+  pl.smem = W * S * (2 * kSub * D * 2) + W * S * 8 + W * S * 4 + 1024;
   pl.warps = W;
   pl.record = Record<D, NT>::kFloats;
   return pl;
@@ -791,15 +844,57 @@ int b2p_decode_simt(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
                     void* out, int64_t out_tok_stride, int64_t out_head_stride, int dtype,
                     int32_t* err_flag, void* stream);
 
-extern "C" int b2p_paged_decode(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
-                                const void* key_cache, const void* value_cache,
-                                int64_t layer_index, int64_t num_layers, int64_t num_slots,
-                                const int32_t* block_tables, int64_t block_table_stride,
-                                const int32_t* context_lens, int num_seqs, int num_q_heads,
-                                int num_kv_heads, int head_dim, int block_size, float scale,
-                                void* out, int64_t out_tok_stride, int64_t out_head_stride,
-                                void* workspace, size_t workspace_size, int dtype,
-                                int32_t* err_flag, void* stream) {
+namespace {
+
+// The newest row of each sequence in append mode (null `k`: plain decode).
+struct AppendRows {
+  const void* k = nullptr;
+  int64_t k_tok = 0, k_head = 0;
+  const void* v = nullptr;
+  int64_t v_tok = 0, v_head = 0;
+};
+
+// CUDA-core path of append mode: puts each sequence's new row at the slot the block table
+// gives for position ctx - 1 (the plain decode kernel then reads it like any other key).
+template <int ES>
+__global__ void append_rows_by_table(AppendRows rows, uint8_t* kpool, uint8_t* vpool,
+                                     const int32_t* bt, int64_t bt_stride, const int32_t* ctx,
+                                     int num_seqs, int64_t layer, int64_t num_slots,
+                                     int block_size, int num_kv_heads, int head_dim,
+                                     int32_t* err) {
+  const int sq = blockIdx.x;
+  if (sq >= num_seqs) return;
+  const int c = ctx[sq];
+  if (c <= 0) return;  // empty history: nothing to append to (decode flags it)
+  const int64_t col = (c - 1) / block_size;
+  const int32_t blk = col < bt_stride ? bt[(int64_t)sq * bt_stride + col] : -1;
+  const int64_t slot = (int64_t)blk * block_size + (c - 1) % block_size;
+  if (blk < 0 || slot >= num_slots) {
+    if (threadIdx.x == 0) set_device_error(err, B2P_DEV_BLOCK_RANGE);
+    return;
+  }
+  const int words = head_dim * ES / 4;  // 4-byte words per head row
+  for (int e = threadIdx.x; e < 2 * num_kv_heads * words; e += blockDim.x) {
+    const bool isv = e >= num_kv_heads * words;
+    const int r = isv ? e - num_kv_heads * words : e;
+    const int h = r / words, w = r - h * words;
+    const uint8_t* src = static_cast<const uint8_t*>(isv ? rows.v : rows.k) +
+                         ((int64_t)sq * (isv ? rows.v_tok : rows.k_tok) +
+                          (int64_t)h * (isv ? rows.v_head : rows.k_head)) * ES;
+    uint8_t* dst = (isv ? vpool : kpool) +
+                   (((layer * num_slots + slot) * num_kv_heads + h) * head_dim) * ES;
+    reinterpret_cast<uint32_t*>(dst)[w] = reinterpret_cast<const uint32_t*>(src)[w];
+  }
+}
+
+int decode_impl(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
+                const void* key_cache, const void* value_cache, int64_t layer_index,
+                int64_t num_layers, int64_t num_slots, const int32_t* block_tables,
+                int64_t block_table_stride, const int32_t* context_lens, int num_seqs,
+                int num_q_heads, int num_kv_heads, int head_dim, int block_size, float scale,
+                void* out, int64_t out_tok_stride, int64_t out_head_stride, void* workspace,
+                size_t workspace_size, int dtype, int32_t* err_flag, void* stream,
+                const AppendRows& app) {
   if (num_seqs < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 ||
       block_size <= 0 || num_slots <= 0 || num_layers <= 0)
     return B2P_EINVAL;
@@ -819,6 +914,27 @@ extern "C" int b2p_paged_decode(const void* q, int64_t q_tok_stride, int64_t q_h
                   ((reinterpret_cast<uintptr_t>(value_cache) & 15u) == 0) &&
                   num_slots <= 0x7fffffffLL && select_plan(dtype, head_dim, group, pl);
   if (!tc) {
+    if (app.k != nullptr) {
+      const int es = dtype == B2P_F32 ? 4 : 2;
+      if ((head_dim * es) % 4 != 0 || dtype < B2P_BF16 || dtype > B2P_F32) return B2P_EINVAL;
+      const cudaStream_t st = static_cast<cudaStream_t>(stream);
+      uint8_t* kp = static_cast<uint8_t*>(const_cast<void*>(key_cache));
+      uint8_t* vp = static_cast<uint8_t*>(const_cast<void*>(value_cache));
+      if (es == 4)
+        append_rows_by_table<4><<<num_seqs, 128, 0, st>>>(app, kp, vp, block_tables,
+                                                          block_table_stride, context_lens,
+                                                          num_seqs, layer_index, num_slots,
+                                                          block_size, num_kv_heads, head_dim,
+                                                          err_flag);
+      else
+        append_rows_by_table<2><<<num_seqs, 128, 0, st>>>(app, kp, vp, block_tables,
+                                                          block_table_stride, context_lens,
+                                                          num_seqs, layer_index, num_slots,
+                                                          block_size, num_kv_heads, head_dim,
+                                                          err_flag);
+      const int rc = b2p_host::check_launch();
+      if (rc != B2P_OK) return rc;
+    }
     return b2p_decode_simt(q, q_tok_stride, q_head_stride, key_cache, value_cache, layer_index,
                            num_layers, num_slots, block_tables, block_table_stride, context_lens,
                            num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, scale, out,
@@ -862,6 +978,15 @@ extern "C" int b2p_paged_decode(const void* q, int64_t q_tok_stride, int64_t q_h
   p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
                                         counters_bytes(num_seqs, num_kv_heads));
   p.err = err_flag;
+  p.new_k = static_cast<const uint8_t*>(app.k);
+  p.nk_tok = app.k_tok;
+  p.nk_head = app.k_head;
+  p.new_v = static_cast<const uint8_t*>(app.v);
+  p.nv_tok = app.v_tok;
+  p.nv_head = app.v_head;
+  p.kpool = static_cast<uint8_t*>(const_cast<void*>(key_cache));
+  p.vpool = static_cast<uint8_t*>(const_cast<void*>(value_cache));
+  p.num_kv_heads = num_kv_heads;
 
   dim3 grid((unsigned)ctas, (unsigned)(num_kv_heads / hpu));
   void* args[] = {&kmap, &vmap, &p};
@@ -869,6 +994,54 @@ extern "C" int b2p_paged_decode(const void* q, int64_t q_tok_stride, int64_t q_h
                                    static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return b2p_host::record_error(e);
   return b2p_host::check_launch();
+}
+
+}  // namespace
+
+extern "C" int b2p_paged_decode(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
+                                const void* key_cache, const void* value_cache,
+                                int64_t layer_index, int64_t num_layers, int64_t num_slots,
+                                const int32_t* block_tables, int64_t block_table_stride,
+                                const int32_t* context_lens, int num_seqs, int num_q_heads,
+                                int num_kv_heads, int head_dim, int block_size, float scale,
+                                void* out, int64_t out_tok_stride, int64_t out_head_stride,
+                                void* workspace, size_t workspace_size, int dtype,
+                                int32_t* err_flag, void* stream) {
+  return decode_impl(q, q_tok_stride, q_head_stride, key_cache, value_cache, layer_index,
+                     num_layers, num_slots, block_tables, block_table_stride, context_lens,
+                     num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, scale, out,
+                     out_tok_stride, out_head_stride, workspace, workspace_size, dtype, err_flag,
+                     stream, AppendRows{});
+}
+
+extern "C" int b2p_paged_decode_append(
+    const void* q, int64_t q_tok_stride, int64_t q_head_stride, const void* new_keys,
+    int64_t k_tok_stride, int64_t k_head_stride, const void* new_values, int64_t v_tok_stride,
+    int64_t v_head_stride, void* key_cache, void* value_cache, int64_t layer_index,
+    int64_t num_layers, int64_t num_slots, const int32_t* block_tables,
+    int64_t block_table_stride, const int32_t* context_lens, int num_seqs, int num_q_heads,
+    int num_kv_heads, int head_dim, int block_size, float scale, void* out,
+    int64_t out_tok_stride, int64_t out_head_stride, void* workspace, size_t workspace_size,
+    int dtype, int32_t* err_flag, void* stream) {
+  if (num_seqs > 0 && (!new_keys || !new_values)) return B2P_EINVAL;
+  // 16-byte rows: the tensor-core path moves each new row as 16-byte pieces.
+  const int es = dtype == B2P_F32 ? 4 : 2;
+  if (((reinterpret_cast<uintptr_t>(new_keys) | reinterpret_cast<uintptr_t>(new_values)) & 15u) ||
+      (k_tok_stride * es) % 16 || (k_head_stride * es) % 16 || (v_tok_stride * es) % 16 ||
+      (v_head_stride * es) % 16)
+    return B2P_EINVAL;
+  AppendRows app;
+  app.k = new_keys;
+  app.k_tok = k_tok_stride;
+  app.k_head = k_head_stride;
+  app.v = new_values;
+  app.v_tok = v_tok_stride;
+  app.v_head = v_head_stride;
+  return decode_impl(q, q_tok_stride, q_head_stride, key_cache, value_cache, layer_index,
+                     num_layers, num_slots, block_tables, block_table_stride, context_lens,
+                     num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, scale, out,
+                     out_tok_stride, out_head_stride, workspace, workspace_size, dtype, err_flag,
+                     stream, app);
 }
 
 // ====================================================================== scratch-free decode

@@ -155,6 +155,58 @@ def paged_decode(
     return out
 
 
+def paged_decode_append(
+    q: torch.Tensor,
+    new_keys: torch.Tensor,
+    new_values: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    layer_index: int,
+    block_tables: torch.Tensor,
+    context_lens: torch.Tensor,
+    block_size: int,
+    scale: float,
+    out: torch.Tensor | None = None,
+    workspace: torch.Tensor | None = None,
+    err_flag: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """K1 + K2 for decode rows in one launch: stores each sequence's new K/V row (position
+    ``context_lens[i] - 1``, slot from its block table) into the pool and attends over the
+    whole history. q: (num_seqs, HQ, D); new_keys / new_values: (num_seqs, Hkv, D)."""
+    _check_pool(key_cache, value_cache)
+    _require_cuda("q", q)
+    _int32("block_tables", block_tables)
+    _int32("context_lens", context_lens)
+    layers, slots, hkv, d = key_cache.shape
+    n, hq, dq = q.shape
+    if dq != d or q.dtype != key_cache.dtype:
+        raise ValueError("q must match the pool's head_dim and dtype")
+    for name, t in (("new_keys", new_keys), ("new_values", new_values)):
+        _require_cuda(name, t)
+        if t.dtype != key_cache.dtype or t.dim() != 3 or t.shape[0] < n or t.shape[1:] != (hkv, d):
+            raise ValueError(f"{name} must be (num_seqs, num_kv_heads, head_dim) in the pool dtype")
+        if t.stride(-1) != 1:
+            raise ValueError(f"{name} must have a contiguous head_dim")
+    if block_tables.dim() != 2 or block_tables.shape[0] < n or context_lens.numel() < n:
+        raise ValueError("block_tables/context_lens must cover every sequence")
+    if out is None:
+        out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    qt, qhs = _tok_head_strides("q", q)
+    ot, ohs = _tok_head_strides("out", out)
+    if workspace is None:
+        workspace = make_decode_workspace(n, hq, hkv, d, q.device)
+    rc = _lib.load().b2p_paged_decode_append(
+        q.data_ptr(), qt, qhs, new_keys.data_ptr(), new_keys.stride(0), new_keys.stride(1),
+        new_values.data_ptr(), new_values.stride(0), new_values.stride(1),
+        key_cache.data_ptr(), value_cache.data_ptr(), layer_index, layers, slots,
+        block_tables.data_ptr(), block_tables.stride(0), context_lens.data_ptr(), n, hq, hkv, d,
+        block_size, float(scale), out.data_ptr(), ot, ohs, workspace.data_ptr(),
+        workspace.numel(), dtype_code(q.dtype), _ptr(err_flag), _stream(q.device),
+    )
+    _lib.check(rc, "b2p_paged_decode_append")
+    return out
+
+
 def paged_prefill(
     q: torch.Tensor,
     key_cache: torch.Tensor,

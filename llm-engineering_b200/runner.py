@@ -12,13 +12,14 @@ Here the same ``ModelRunner.forward(executions) -> (B, vocab)`` interface
     the GPU from a per-step descriptor (query length, key length, table row per execution)
     and the step's block tables;
   * ``B200PagedCache.update`` (the HF ``Cache`` hook, transformers/models/qwen2/
-    modeling_qwen2.py:225): K1 writes the step's K/V rows into the pool and returns
-    without gathering anything;
+    modeling_qwen2.py:225): K1 writes the step's prefill K/V rows into the pool and
+    returns without gathering anything;
   * ``paged_attention`` (registered with HF's ``AttentionInterface`` under
-    ``ATTENTION_NAME``; the model calls it at modeling_qwen2.py:227-240): K2 for the
-    leading decode executions and K3 for the prefill / chunked-prefill ones, reading the
-    pool in place through block tables. A registered name outside HF's mask registry also
-    makes HF skip building any mask.
+    ``ATTENTION_NAME``; the model calls it at modeling_qwen2.py:227-240): the fused K1 + K2
+    call for the leading decode executions (it stores their new K/V rows and attends in one
+    launch) and K3 for the prefill / chunked-prefill ones, reading the pool in place
+    through block tables. A registered name outside HF's mask registry also makes HF skip
+    building any mask.
   * ``logits_to_keep`` restricts the LM head to each execution's last query row, which is
     exactly the rows the reference keeps with ``index_select`` (paged_model_runner.py:85-91).
 
@@ -70,6 +71,9 @@ class StepBatch:
     logit_indices: torch.Tensor  # int64 [B]
     workspace: torch.Tensor
     err: torch.Tensor
+    # Decode rows take the fused K1 + K2 call: the cache hook then writes only the
+    # prefill rows, and the attention function stores the decode rows' new K/V itself.
+    fused_decode: bool = False
 
 
 def _phase_of(execution) -> str:
@@ -84,11 +88,12 @@ def paged_attention(module: torch.nn.Module, query: torch.Tensor, key: torch.Ten
                     dropout: float = 0.0, scaling: float | None = None, **kwargs: Any):
     """HF attention-interface function: paged attention of the packed query rows.
 
-    query: (1, HQ, Tq, D) after RoPE. ``key``/``value`` are this step's new rows (already
-    written to the pool by ``B200PagedCache.update``); the kernels read every history
-    from the pool. Returns (attn_output (1, Tq, HQ, D), None) like HF's SDPA path.
+    query: (1, HQ, Tq, D) after RoPE. ``key``/``value`` are this step's new rows; the
+    prefill rows are already in the pool (``B200PagedCache.update``), and the decode rows
+    are stored by the fused decode call when the step uses it. The kernels read every
+    history from the pool. Returns (attn_output (1, Tq, HQ, D), None) like HF's SDPA path.
     """
-    del key, value, attention_mask, kwargs
+    del attention_mask, kwargs
     batch = _active_batch.get()
     if batch is None:
         raise RuntimeError(f"{ATTENTION_NAME} attention used outside B200PagedModelRunner.forward")
@@ -101,7 +106,12 @@ def paged_attention(module: torch.nn.Module, query: torch.Tensor, key: torch.Ten
     k = batch.kernels
     out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
     nd = batch.num_decode
-    if nd:
+    if nd and batch.fused_decode:
+        k.paged_decode_append(q[:nd], key[0].transpose(0, 1)[:nd], value[0].transpose(0, 1)[:nd],
+                              batch.key_cache, batch.value_cache, layer, batch.block_tables[:nd],
+                              batch.context_lens[:nd], batch.block_size, scaling, out=out[:nd],
+                              workspace=batch.workspace, err_flag=batch.err)
+    elif nd:
         k.paged_decode(q[:nd], batch.key_cache, batch.value_cache, layer, batch.block_tables[:nd],
                        batch.context_lens[:nd], batch.block_size, scaling, out=out[:nd],
                        workspace=batch.workspace, err_flag=batch.err)
@@ -119,8 +129,9 @@ def _register_attention() -> None:
 
 
 class B200PagedCache(Cache):
-    """HF cache hook: writes each layer's new K/V rows into the pool (K1) and returns the
-    states unchanged — there is no gathered history to hand back."""
+    """HF cache hook: writes each layer's new prefill K/V rows into the pool (K1; decode
+    rows are stored by the fused decode call) and returns the states unchanged — there is
+    no gathered history to hand back."""
 
     def __init__(self, batch: StepBatch) -> None:
         super().__init__(layers=[])
@@ -142,9 +153,11 @@ class B200PagedCache(Cache):
                 "Packed KV query length does not match BatchLayout: "
                 f"expected {self._batch.total_q}, got {key_states.shape[2]}.")
         b = self._batch
-        b.kernels.kv_write(b.key_cache, b.value_cache, layer_idx, b.slot_mapping,
-                           key_states[0].transpose(0, 1), value_states[0].transpose(0, 1),
-                           b.err)
+        first = b.num_decode if b.fused_decode else 0  # decode rows: stored by the fused call
+        if first < b.total_q:
+            b.kernels.kv_write(b.key_cache, b.value_cache, layer_idx, b.slot_mapping[first:],
+                               key_states[0].transpose(0, 1)[first:],
+                               value_states[0].transpose(0, 1)[first:], b.err)
         return key_states, value_states
 
     def get_seq_length(self, layer_idx: int = 0) -> int:
@@ -287,7 +300,8 @@ class B200PagedModelRunner:
             num_execs=n, num_decode=num_decode, max_q_len=max(d["qlens"]),
             slot_mapping=md["slot_mapping"], positions=md["positions"],
             cu_seqlens_q=md["cu_seqlens_q"], context_lens=ctx, block_tables=tables,
-            logit_indices=md["logit_indices"], workspace=self._workspace, err=self._err)
+            logit_indices=md["logit_indices"], workspace=self._workspace, err=self._err,
+            fused_decode=num_decode > 0 and hasattr(self._kernels, "paged_decode_append"))
         return batch, input_ids
 
     # ------------------------------------------------------------------ ModelRunner

@@ -26,9 +26,9 @@ def scatter(key_cache: torch.Tensor, value_cache: torch.Tensor, layer: int,
         raise ValueError("layer_index must be within the configured layers.")
     if any(s < 0 or s >= num_slots for s in slot_ids):
         raise ValueError("slot_ids must be within the configured physical slots.")
-    idx = torch.as_tensor(list(slot_ids), dtype=torch.long)
-    key_cache[layer].index_copy_(0, idx, keys)
-    value_cache[layer].index_copy_(0, idx, values)
+    idx = torch.as_tensor(list(slot_ids), dtype=torch.long, device=key_cache.device)
+    key_cache[layer].index_copy_(0, idx, keys.to(key_cache.device))
+    value_cache[layer].index_copy_(0, idx, values.to(value_cache.device))
 
 
 def gather(key_cache: torch.Tensor, value_cache: torch.Tensor, layer: int,
@@ -40,7 +40,7 @@ def gather(key_cache: torch.Tensor, value_cache: torch.Tensor, layer: int,
         raise ValueError("layer_index must be within the configured layers.")
     if any(s < 0 or s >= num_slots for s in slot_ids):
         raise ValueError("slot_ids must be within the configured physical slots.")
-    idx = torch.as_tensor(list(slot_ids), dtype=torch.long)
+    idx = torch.as_tensor(list(slot_ids), dtype=torch.long, device=key_cache.device)
     return key_cache[layer].index_select(0, idx), value_cache[layer].index_select(0, idx)
 
 

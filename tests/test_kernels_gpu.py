@@ -269,6 +269,43 @@ def test_decode_full_benchmark_workload(ops):
     close(out, expect, torch.bfloat16)
 
 
+@pytest.mark.parametrize("shape,dtype", [((12, 2, 128, 16), torch.bfloat16),
+                                         ((28, 4, 128, 16), torch.bfloat16),
+                                         ((12, 2, 128, 32), torch.float16),
+                                         ((14, 2, 64, 16), torch.bfloat16),
+                                         ((14, 2, 64, 16), torch.float32)])
+def test_decode_append_equals_write_then_decode(ops, shape, dtype):
+    """The fused call stores the same pool rows as K1 with the block-table slot mapping and
+    returns exactly what K2 returns after that write (the CUDA-core fallback for fp32)."""
+    hq, hkv, d, bs = shape
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(41)
+    ctx = [1, 16, 17, 32, 100, 511, 512, 1024, 2049] + rng.integers(1, 3000, size=120).tolist()
+    nb = sum((c + bs - 1) // bs for c in ctx) + 5
+    kc, vc = make_pool(42, 2, nb, bs, hkv, d, dtype)
+    tables, bt = make_tables(43, ctx, bs, nb)
+    g = torch.Generator().manual_seed(44)
+    q = torch.randn(len(ctx), hq, d, generator=g).to(dtype).to(dev)
+    new_k = torch.randn(len(ctx), hkv, d, generator=g).to(dtype).to(dev)
+    new_v = torch.randn(len(ctx), hkv, d, generator=g).to(dtype).to(dev)
+    slots = torch.tensor([t[(c - 1) // bs] * bs + (c - 1) % bs for t, c in zip(tables, ctx)],
+                         dtype=torch.int32, device=dev)
+    ctx_d = torch.tensor(ctx, dtype=torch.int32, device=dev)
+    ka, va = kc.to(dev), vc.to(dev)
+    kb, vb = ka.clone(), va.clone()
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ops.kv_write(ka, va, 1, slots, new_k, new_v, err)
+    out_a = ops.paged_decode(q, ka, va, 1, bt.to(dev), ctx_d, bs, d ** -0.5, err_flag=err)
+    out_b = ops.paged_decode_append(q, new_k, new_v, kb, vb, 1, bt.to(dev), ctx_d, bs, d ** -0.5,
+                                    err_flag=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(ka, kb) and torch.equal(va, vb)
+    assert torch.equal(out_a, out_b)
+    ref.scatter(kc, vc, 1, slots.tolist(), new_k.cpu(), new_v.cpu())
+    close(out_b, ref.decode_attention(q.cpu(), kc, vc, 1, tables, ctx, bs, d ** -0.5), dtype)
+
+
 def churned_tables(rng, ctx, bs, num_blocks, churn=0.3):
     """Block tables after allocation churn: blocks are handed out from a FIFO free list,
     30% of them are freed in random order and handed out again, so every table mixes

@@ -47,6 +47,17 @@ class CpuKernels:
         out.copy_(res.to(out.dtype))
         return out
 
+    def paged_decode_append(self, q, new_k, new_v, kc, vc, layer, bt, ctx, bs, scale, out=None,
+                            workspace=None, err_flag=None):
+        n = q.shape[0]
+        for i in range(n):  # the new row goes to the slot of position ctx - 1
+            pos = int(ctx[i]) - 1
+            slot = int(bt[i, pos // bs]) * bs + pos % bs
+            kc[layer][slot] = new_k[i]
+            vc[layer][slot] = new_v[i]
+        return self.paged_decode(q, kc, vc, layer, bt, ctx, bs, scale, out=out,
+                                 workspace=workspace, err_flag=err_flag)
+
     def paged_prefill(self, q, kc, vc, layer, bt, cu, ctx, max_q, bs, scale, out=None,
                       err_flag=None, num_rows=None):
         cu_l = cu.tolist()

@@ -6,8 +6,10 @@
   for token by this package's engine + B200PagedModelRunner on the GPU.
 * Logits, bf16: a 2-layer model with the Qwen2.5-1.5B attention shape (12/2 heads,
   head_dim 128) against the reference-style packed runner (gather + dense mask + SDPA)
-  run in fp32 on the same weights: per-step logits within max-abs 5e-2 (bf16 weights and
-  activations), top-1 agreement on every row where the fp32 margin exceeds 5e-2.
+  run in fp32 on the same weights. The bf16 error budget is that of the reference path
+  itself: the same packed runner run in bf16 on the GPU sets it, and this package's logits
+  must stay within 1.5x of its max-abs error (and never above 0.1); top-1 agreement on
+  every row where the fp32 margin exceeds 5e-2.
 """
 
 from __future__ import annotations
@@ -88,6 +90,10 @@ def test_bf16_runner_logits_match_reference_path():
     kr = torch.zeros(2, blocks * bs, 2, 128)
     vr = torch.zeros(2, blocks * bs, 2, 128)
     reference = ReferencePackedRunner(ref_model, kr, vr, bs)
+    # the reference path itself in bf16 (GPU): its distance from fp32 is the bf16 budget
+    kb = torch.zeros(2, blocks * bs, 2, 128, dtype=torch.bfloat16, device=dev)
+    reference_bf16 = ReferencePackedRunner(copy.deepcopy(base).to(dev, torch.bfloat16), kb,
+                                           torch.zeros_like(kb), bs)
     rng = np.random.default_rng(9)
     requests = [eng.Request(request_id=f"r{i}",
                             prompt_token_ids=tuple(int(x) for x in rng.integers(0, 1000, size=n)),
@@ -101,13 +107,15 @@ def test_bf16_runner_logits_match_reference_path():
 
         def __init__(self):
             self.max_err = 0.0
+            self.budget = 0.0
             self.checked = 0
 
         def forward(self, executions):
             want = reference.forward(executions)
             got = ours.forward(executions).float().cpu()
-            err = (got - want).abs().max().item()
-            self.max_err = max(self.max_err, err)
+            torch_bf16 = reference_bf16.forward(executions).float().cpu()
+            self.max_err = max(self.max_err, (got - want).abs().max().item())
+            self.budget = max(self.budget, (torch_bf16 - want).abs().max().item())
             top2 = torch.topk(want, 2, dim=-1).values
             confident = (top2[:, 0] - top2[:, 1]) > 5e-2
             agree = got.argmax(-1) == want.argmax(-1)
@@ -123,7 +131,8 @@ def test_bf16_runner_logits_match_reference_path():
     engine.run_until_complete()
     assert runner.device_error() == 0
     assert both.checked > 6
-    assert both.max_err < 5e-2, both.max_err
+    assert both.max_err <= max(1.5 * both.budget, 2e-2) and both.max_err < 0.1, \
+        (both.max_err, both.budget)
 
 
 def test_chunked_prefill_slices_in_a_mixed_step_match_whole_prefill():
