@@ -23,6 +23,8 @@
 //
 // Warp roles (192 threads): warp 0 = TMA producer, warp 1 = tensor-memory owner and MMA
 // issuer (one thread), warps 2..5 = softmax + epilogue (thread = TMEM lane = query row).
+#include <atomic>
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -39,6 +41,8 @@ constexpr int kSub = 16;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct PrefillParams {
+  int hq;                  // query heads
+  int32_t* ctr;            // {next work item, CTAs done}: zero at launch, re-zeroed at the end
   const int32_t* block_tables;
   int64_t bt_stride;
   const int32_t* cu_q;
@@ -61,10 +65,12 @@ constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kQBytes;       // 2 stages
 constexpr int kOffV = kOffK + 2 * kKVBytes;  // 2 stages
 constexpr int kOffBar = kOffV + 2 * kKVBytes;
-constexpr int kNumBars = 1 + 2 * 6;          // q_full, k_full[2], v_full[2], kv_empty[2],
-                                             // s_full[2], p_full[2], o_done[2]
-constexpr int kOffMisc = kOffBar + kNumBars * 8 + 8;  // + mma_done
-constexpr int kSmemBytes = kOffMisc + 64;
+constexpr int kNumBars = 1 + 2 * 6 + 1 + 1 + 4;  // q_full, k_full[2], v_full[2], kv_empty[2],
+                                                // s_full[2], p_full[2], o_done[2], mma_done,
+                                                // q_empty, item_full[2], item_empty[2]
+constexpr int kOffMisc = kOffBar + kNumBars * 8;
+constexpr int kOffItems = kOffMisc + 64;
+constexpr int kSmemBytes = kOffItems + 2 * 48;
 
 // TMEM columns: S buffers at 0 and 64, O at 128 (256 allocated).
 constexpr uint32_t kTmemCols = 256;
@@ -203,35 +209,65 @@ __device__ __forceinline__ float row_exp64(const uint32_t (&r0)[32], const uint3
   return s0 + s1;
 }
 
-// Work item k -> (sequence, query tile), tiles of a sequence enumerated last first (the
-// last tiles see the most keys, so they start early). One warp; all lanes return it.
-__device__ bool find_item(const PrefillParams& p, int k, int& seq, int& tile) {
-  const int lane = threadIdx.x & 31;
-  int run = 0;
-  for (int base = 0; base < p.num_seqs; base += 32) {
-    const int i = base + lane;
-    int nt = 0;
-    if (i < p.num_seqs) nt = ceil_div(max(__ldg(p.cu_q + i + 1) - __ldg(p.cu_q + i), 0), kM);
-    int incl = nt;
+// Work items. Sequence s has ntiles(s) = ceil(q_len_s / 128) query tiles; tile-items are
+// ordered round by round from the end: round r holds tile ntiles(s) - 1 - r of every
+// sequence with more than r tiles, sequences in index order. A sequence's later tiles see
+// more keys, so the order runs close to longest first (LPT) whatever the prompt mix. Work
+// item k is tile-item k / HQ for query head k % HQ: the query heads of one tile are
+// neighbours, so the heads of a GQA group, which read the same K/V tiles, run together and
+// share them through L2.
+struct ItemInfo {
+  int seq;  // -1: no more work for this CTA
+  int qt, qh, q0, qlen, ctx, rows_valid, pos0, n_kv, pad[3];
+};
+
+__device__ __forceinline__ int ntiles_of(const PrefillParams& p, int s) {
+  const int q = __ldg(p.cu_q + s + 1) - __ldg(p.cu_q + s);
+  return q > 0 ? ceil_div(q, kM) : 0;
+}
+
+__device__ __forceinline__ int64_t warp_sum64(int64_t v) {
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
-    }
-    const unsigned hit = __ballot_sync(0xffffffffu, run + incl > k);
-    if (hit) {
-      const int src = __ffs(hit) - 1;
-      const int lo = run + __shfl_sync(0xffffffffu, incl - nt, src);
-      const int cnt = __shfl_sync(0xffffffffu, nt, src);
-      seq = base + src;
-      tile = cnt - 1 - (k - lo);
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Tile-items in rounds before r: sum over sequences of min(ntiles, r). One warp.
+__device__ int64_t items_before_round(const PrefillParams& p, int r, int lane) {
+  int64_t acc = 0;
+  for (int s = lane; s < p.num_seqs; s += 32) acc += min(ntiles_of(p, s), r);
+  return warp_sum64(acc);
+}
+
+// Tile-item t -> (sequence, query tile). One warp; all lanes get the result.
+__device__ bool decode_tile_item(const PrefillParams& p, int64_t t, int maxnt, int lane,
+                                 int& seq, int& tile) {
+  int lo = 0, hi = maxnt - 1;  // largest r with items_before_round(r) <= t
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (items_before_round(p, mid, lane) <= t) lo = mid; else hi = mid - 1;
+  }
+  int64_t i = t - items_before_round(p, lo, lane);
+  for (int base = 0; base < p.num_seqs; base += 32) {
+    const int s = base + lane;
+    const int nt = s < p.num_seqs ? ntiles_of(p, s) : 0;
+    const unsigned m = __ballot_sync(0xffffffffu, nt > lo);
+    const int c = __popc(m);
+    if (i < c) {
+      const int pos = __fns(m, 0, (int)i + 1);
+      seq = base + pos;
+      tile = __shfl_sync(0xffffffffu, nt, pos) - 1 - lo;
       return true;
     }
-    run += __shfl_sync(0xffffffffu, incl, 31);
+    i -= c;
   }
   return false;
 }
 
+// Persistent CTAs (two per SM) claim work items in the order above from an atomic counter
+// (dynamic, so faster SMs take more items and the short items come last). Tensor memory, barriers and descriptors are set up once; the stage, S-buffer and
+// item counters run on across items, so the next item's Q and first K/V tiles load while
+// the current item finishes, and its first QK^T MMAs run during the current epilogue.
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_constant__ CUtensorMap qmap,
                                                                 const __grid_constant__ CUtensorMap kmap,
@@ -249,51 +285,36 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
   uint64_t* p_full = bars + 9;
   uint64_t* o_done = bars + 11;
   uint64_t* mma_done = bars + 13;
+  uint64_t* q_empty = bars + 14;
+  uint64_t* item_full = bars + 15;
+  uint64_t* item_empty = bars + 17;
   int32_t* misc = reinterpret_cast<int32_t*>(smem + kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 5);
+  ItemInfo* items = reinterpret_cast<ItemInfo*>(smem + kOffItems);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int qh = blockIdx.y;
-  const int kvh = qh / p.group;
-
-  if (warp == 0) {
-    int seq = -1, tile = 0;
-    const bool ok = find_item(p, (int)blockIdx.x, seq, tile);
-    if (lane == 0) {
-      misc[0] = ok ? seq : -1;
-      misc[1] = tile;
-      *abort_flag = 0;
-      if (ok) {
-        mbar_init(q_full, 1);
-        for (int s = 0; s < 2; ++s) {
-          mbar_init(&k_full[s], 1);
-          mbar_init(&v_full[s], 1);
-          mbar_init(&kv_empty[s], 1);
-          mbar_init(&s_full[s], 1);
-          mbar_init(&p_full[s], kM);
-          mbar_init(&o_done[s], 1);
-        }
-        mbar_init(mma_done, 1);
-        fence_mbar_init();
-      }
-    }
-  }
-  __syncthreads();
-  const int seq = misc[0];
-  if (seq < 0) return;  // grid is an upper bound on the number of tiles
-  const int qt = misc[1];
-  const int q0 = __ldg(p.cu_q + seq);
-  const int qlen = __ldg(p.cu_q + seq + 1) - q0;
-  const int ctx = __ldg(p.ctx + seq);
-  const int rows_valid = min(kM, qlen - qt * kM);
-  const int pos0 = ctx - qlen + qt * kM;            // position of the tile's first row
-  const int last_pos = pos0 + rows_valid - 1;
-  const int n_kv = last_pos >= 0 ? ceil_div(last_pos + 1, kN) : 0;
-  if (threadIdx.x == 0 && (ctx < qlen || n_kv == 0)) set_device_error(p.err, B2P_DEV_LENGTH);
   const uint32_t ab = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
 
+  if (warp == 0 && lane == 0) {
+    *abort_flag = 0;
+    misc[0] = misc[1] = misc[2] = 0;
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&p_full[s], kM);
+      mbar_init(&o_done[s], 1);
+      mbar_init(&item_full[s], 1);
+      mbar_init(&item_empty[s], 5);  // the MMA issuer and the four softmax warps
+    }
+    mbar_init(mma_done, 1);
+    mbar_init(q_empty, 1);
+    fence_mbar_init();
+  }
   if (warp == 1) {  // tensor memory for S0, S1, O
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
@@ -305,120 +326,225 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
 
+  // An item as seen by the consumer warps: wait for its slot, copy it, hand the slot back.
+  auto take_item = [&](int i, ItemInfo& it) -> bool {
+    const int b = i & 1;
+    bool ok = true;
+    if (lane == 0) ok = mbar_wait_bounded(&item_full[b], (uint32_t)((i >> 1) & 1), p.err);
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    if (!ok) {
+      *abort_flag = 1;
+      return false;
+    }
+    __syncwarp();
+    it = items[b];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&item_empty[b]);
+    return it.seq >= 0;
+  };
+
   if (warp == 0) {
-    // ---------------------------------------------------------------- producer
+    // ---------------------------------------------------------------- scheduler + producer
+    int64_t total = 0;
+    int maxnt = 0;
+    for (int s = lane; s < p.num_seqs; s += 32) {
+      const int nt = ntiles_of(p, s);
+      total += nt;
+      maxnt = max(maxnt, nt);
+    }
+    total = warp_sum64(total);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) maxnt = max(maxnt, __shfl_xor_sync(0xffffffffu, maxnt, o));
+    const int64_t n_items = total * p.hq;
     const int spb = p.block_size / kSub;
     const int64_t num_slots = p.num_blocks * p.block_size;
-    const int32_t* bt = p.block_tables + (int64_t)seq * p.bt_stride;
     if (lane == 0) {
       tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
-      mbar_arrive_expect_tx(q_full, kQBytes);
-      for (int c = 0; c < 2; ++c)
-        tma_load_4d(smem + kOffQ + c * (kM * 128), &qmap, q_full, 0, c, qh, q0 + qt * kM);
     }
-    // lane l holds the slot of sub-block (win + l); 8 KV tiles per window
-    int win = -32;
-    int64_t my_slot = 0;
+    int64_t g = 0;  // K/V tiles issued by this CTA (stage = g & 1)
+    int nq = 0;     // Q tiles issued
     bool aborted = false;
-    int last_issued = -1;
-    for (int j = 0; j < n_kv && !aborted; ++j) {
-      const int s = j & 1;
-      if (j * 4 >= win + 32) {
-        win = j * 4;
-        const int sb = win + lane;  // sub-block index within the sequence
-        const int64_t col = sb / spb;
-        int32_t blk = -1;
-        if ((int64_t)sb * kSub < ctx && col < p.bt_stride) blk = __ldg(bt + col);
-        if ((int64_t)sb * kSub < ctx && (blk < 0 || (int64_t)blk >= p.num_blocks)) {
-          set_device_error(p.err, B2P_DEV_BLOCK_RANGE);
-          blk = -1;
+    // Claims run one item ahead: the next item's claim is in flight while this one's tiles
+    // are issued.
+    int32_t claim = 0;
+    if (lane == 0) claim = atomicAdd(p.ctr, 1);
+    for (int i = 0;; ++i) {
+      const int64_t k = __shfl_sync(0xffffffffu, claim, 0);
+      ItemInfo it;
+      it.seq = -1;
+      if (k < n_items && !aborted) {
+        int seq = 0, tile = 0;
+        if (decode_tile_item(p, k / p.hq, maxnt, lane, seq, tile)) {
+          it.seq = seq;
+          it.qt = tile;
+          it.qh = (int)(k % p.hq);
+          it.q0 = __ldg(p.cu_q + seq);
+          it.qlen = __ldg(p.cu_q + seq + 1) - it.q0;
+          it.ctx = __ldg(p.ctx + seq);
+          it.rows_valid = min(kM, it.qlen - tile * kM);
+          it.pos0 = it.ctx - it.qlen + tile * kM;  // position of the tile's first row
+          const int last_pos = it.pos0 + it.rows_valid - 1;
+          it.n_kv = last_pos >= 0 ? ceil_div(last_pos + 1, kN) : 0;
+          if (lane == 0 && (it.ctx < it.qlen || it.n_kv == 0)) set_device_error(p.err, B2P_DEV_LENGTH);
         }
-        my_slot = blk < 0 ? num_slots : (int64_t)blk * p.block_size + (int64_t)(sb % spb) * kSub;
       }
-      int64_t slots[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) slots[u] = __shfl_sync(0xffffffffu, my_slot, j * 4 - win + u);
+      const int b = i & 1;
+      bool ok = true;
       if (lane == 0) {
-        if (j >= 2 && !mbar_wait_bounded(&kv_empty[s], (uint32_t)(((j >> 1) - 1) & 1), p.err)) {
+        if (i >= 2) ok = mbar_wait_bounded(&item_empty[b], (uint32_t)(((i >> 1) - 1) & 1), p.err);
+        if (ok) {
+          items[b] = it;
+          mbar_arrive(&item_full[b]);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) {
+        *abort_flag = 1;
+        aborted = true;
+      }
+      if (it.seq < 0 || aborted) break;
+      if (lane == 0) claim = atomicAdd(p.ctr, 1);
+      if (it.n_kv == 0) continue;
+      const int kvh = it.qh / p.group;
+      if (lane == 0) {
+        // The previous item's QK^T MMAs are done with the Q buffer before it is refilled.
+        if (nq >= 1 && !mbar_wait_bounded(q_empty, (uint32_t)((nq - 1) & 1), p.err)) {
           *abort_flag = 1;
           aborted = true;
-        } else if (*abort_flag) {
-          aborted = true;
         } else {
-          uint8_t* kdst = smem + kOffK + s * kKVBytes;
-          uint8_t* vdst = smem + kOffV + s * kKVBytes;
-          mbar_arrive_expect_tx(&k_full[s], kKVBytes);
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-#pragma unroll
-            for (int c = 0; c < 2; ++c)
-              tma_load_5d(kdst + c * (kN * 128) + u * (kSub * 128), &kmap, &k_full[s], 0, c, kvh,
-                          (int)slots[u], p.layer);
-          mbar_arrive_expect_tx(&v_full[s], kKVBytes);
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-#pragma unroll
-            for (int c = 0; c < 2; ++c)
-              tma_load_5d(vdst + c * (kN * 128) + u * (kSub * 128), &vmap, &v_full[s], 0, c, kvh,
-                          (int)slots[u], p.layer);
-          last_issued = j;
+          mbar_arrive_expect_tx(q_full, kQBytes);
+          for (int c = 0; c < 2; ++c)
+            tma_load_4d(smem + kOffQ + c * (kM * 128), &qmap, q_full, 0, c, it.qh,
+                        it.q0 + it.qt * kM);
+          misc[1] = nq + 1;  // Q tiles issued
         }
       }
       aborted = __shfl_sync(0xffffffffu, aborted ? 1 : 0, 0) != 0;
+      if (aborted) break;
+      ++nq;
+      const int32_t* bt = p.block_tables + (int64_t)it.seq * p.bt_stride;
+      // lane l holds the slot of sub-block (win + l); 8 KV tiles per window
+      int win = -32;
+      int64_t my_slot = 0;
+      for (int j = 0; j < it.n_kv && !aborted; ++j, ++g) {
+        const int s = (int)(g & 1);
+        if (j * 4 >= win + 32) {
+          win = j * 4;
+          const int sb = win + lane;  // sub-block index within the sequence
+          const int64_t col = sb / spb;
+          int32_t blk = -1;
+          if ((int64_t)sb * kSub < it.ctx && col < p.bt_stride) blk = __ldg(bt + col);
+          if ((int64_t)sb * kSub < it.ctx && (blk < 0 || (int64_t)blk >= p.num_blocks)) {
+            set_device_error(p.err, B2P_DEV_BLOCK_RANGE);
+            blk = -1;
+          }
+          my_slot = blk < 0 ? num_slots : (int64_t)blk * p.block_size + (int64_t)(sb % spb) * kSub;
+        }
+        int64_t slots[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) slots[u] = __shfl_sync(0xffffffffu, my_slot, j * 4 - win + u);
+        if (lane == 0) {
+          if (g >= 2 && !mbar_wait_bounded(&kv_empty[s], (uint32_t)(((g >> 1) - 1) & 1), p.err)) {
+            *abort_flag = 1;
+            aborted = true;
+          } else if (*abort_flag) {
+            aborted = true;
+          } else {
+            uint8_t* kdst = smem + kOffK + s * kKVBytes;
+            uint8_t* vdst = smem + kOffV + s * kKVBytes;
+            mbar_arrive_expect_tx(&k_full[s], kKVBytes);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+              for (int c = 0; c < 2; ++c)
+                tma_load_5d(kdst + c * (kN * 128) + u * (kSub * 128), &kmap, &k_full[s], 0, c,
+                            kvh, (int)slots[u], p.layer);
+            mbar_arrive_expect_tx(&v_full[s], kKVBytes);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+              for (int c = 0; c < 2; ++c)
+                tma_load_5d(vdst + c * (kN * 128) + u * (kSub * 128), &vmap, &v_full[s], 0, c,
+                            kvh, (int)slots[u], p.layer);
+            misc[2] = (int)(g + 1);  // K/V tiles issued
+          }
+        }
+        aborted = __shfl_sync(0xffffffffu, aborted ? 1 : 0, 0) != 0;
+      }
+      if (aborted) break;
     }
-    if (lane == 0) misc[2] = last_issued;
+    if (aborted && lane == 0) {  // the consumers learn it from the flag or their waits
+      *abort_flag = 1;
+    }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0 && n_kv > 0) {
-      const uint32_t id_qk = idesc_f16(ab, kM, kN, 0, 0);
-      const uint32_t id_pv = idesc_f16(ab, kM, kD, 0, 1);
-      const uint32_t q_addr = smem_u32(smem + kOffQ);
-      bool ok = mbar_wait_bounded(q_full, 0, p.err);
-      auto issue_qk = [&](int j) {
-        const int s = j & 1;
-        const uint32_t k_addr = smem_u32(smem + kOffK + s * kKVBytes);
-        const uint32_t d = tbase + (s ? kColS1 : kColS0);
+    const uint32_t id_qk = idesc_f16(ab, kM, kN, 0, 0);
+    const uint32_t id_pv = idesc_f16(ab, kM, kD, 0, 1);
+    const uint32_t q_addr = smem_u32(smem + kOffQ);
+    int64_t g = 0;
+    int nq = 0;
+    bool ok = true;
+    for (int i = 0; ok; ++i) {
+      ItemInfo it;
+      if (!take_item(i, it)) break;
+      if (it.n_kv == 0) continue;
+      if (lane == 0) {
+        auto issue_qk = [&](int64_t gg) {
+          const int s = (int)(gg & 1);
+          const uint32_t k_addr = smem_u32(smem + kOffK + s * kKVBytes);
+          const uint32_t d = tbase + (s ? kColS1 : kColS0);
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint64_t da = smem_desc_sw128(q_addr + (kk >> 2) * (kM * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t db = smem_desc_sw128(k_addr + (kk >> 2) * (kN * 128) + (kk & 3) * 32, 16, 1024);
-          mma_ss(d, da, db, id_qk, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < kD / 16; ++kk) {
+            const uint64_t da = smem_desc_sw128(q_addr + (kk >> 2) * (kM * 128) + (kk & 3) * 32, 16, 1024);
+            const uint64_t db = smem_desc_sw128(k_addr + (kk >> 2) * (kN * 128) + (kk & 3) * 32, 16, 1024);
+            mma_ss(d, da, db, id_qk, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(&s_full[s]);
+        };
+        // S buffer g & 1 held P of tile g - 2: PV(g - 2) must be done reading it.
+        auto s_free = [&](int64_t gg) -> bool {
+          return gg < 2 || mbar_wait_bounded(&o_done[(gg - 2) & 1], (uint32_t)(((gg - 2) >> 1) & 1), p.err);
+        };
+        ok = mbar_wait_bounded(q_full, (uint32_t)(nq & 1), p.err);
+        if (ok) ok = s_free(g) && mbar_wait_bounded(&k_full[g & 1], (uint32_t)((g >> 1) & 1), p.err);
+        if (ok) {
+          tc_fence_after();
+          issue_qk(g);
+          if (it.n_kv == 1) mma_commit(q_empty);  // the item's last read of Q
         }
-        mma_commit(&s_full[s]);
-      };
-      if (ok) ok = mbar_wait_bounded(&k_full[0], 0, p.err);
-      if (ok) {
-        tc_fence_after();
-        issue_qk(0);
-      }
-      for (int j = 0; j < n_kv && ok && !*abort_flag; ++j) {
-        const int s = j & 1;
-        if (j + 1 < n_kv) {
-          const int s1 = (j + 1) & 1;
-          // S buffer s1 held P(j-1): PV(j-1) must be done reading it.
-          if (j >= 1) ok = mbar_wait_bounded(&o_done[(j - 1) & 1], (uint32_t)(((j - 1) >> 1) & 1), p.err);
-          if (ok) ok = mbar_wait_bounded(&k_full[s1], (uint32_t)(((j + 1) >> 1) & 1), p.err);
+        for (int j = 0; j < it.n_kv && ok && !*abort_flag; ++j, ++g) {
+          const int s = (int)(g & 1);
+          if (j + 1 < it.n_kv) {
+            ok = s_free(g + 1) &&
+                 mbar_wait_bounded(&k_full[(g + 1) & 1], (uint32_t)(((g + 1) >> 1) & 1), p.err);
+            if (!ok) break;
+            tc_fence_after();
+            issue_qk(g + 1);
+            if (j + 2 == it.n_kv) mma_commit(q_empty);
+          }
+          ok = mbar_wait_bounded(&p_full[s], (uint32_t)((g >> 1) & 1), p.err);
+          if (ok) ok = mbar_wait_bounded(&v_full[s], (uint32_t)((g >> 1) & 1), p.err);
           if (!ok) break;
           tc_fence_after();
-          issue_qk(j + 1);
-        }
-        ok = mbar_wait_bounded(&p_full[s], (uint32_t)((j >> 1) & 1), p.err);
-        if (ok) ok = mbar_wait_bounded(&v_full[s], (uint32_t)((j >> 1) & 1), p.err);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t v_addr = smem_u32(smem + kOffV + s * kKVBytes);
-        const uint32_t p_tmem = tbase + (s ? kColS1 : kColS0);
+          const uint32_t v_addr = smem_u32(smem + kOffV + s * kKVBytes);
+          const uint32_t p_tmem = tbase + (s ? kColS1 : kColS0);
 #pragma unroll
-        for (int kk = 0; kk < kN / 16; ++kk) {
-          const uint64_t db = smem_desc_sw128(v_addr + kk * (16 * 128), kN * 128, 1024);
-          mma_ts(tbase + kColO, p_tmem + kk * 8, db, id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kN / 16; ++kk) {
+            const uint64_t db = smem_desc_sw128(v_addr + kk * (16 * 128), kN * 128, 1024);
+            mma_ts(tbase + kColO, p_tmem + kk * 8, db, id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&kv_empty[s]);
+          mma_commit(&o_done[s]);
         }
-        mma_commit(&kv_empty[s]);
-        mma_commit(&o_done[s]);
+        if (!ok) *abort_flag = 1;
       }
-      if (!ok) *abort_flag = 1;
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      g = __shfl_sync(0xffffffffu, g, 0);
+      ++nq;
+    }
+    if (lane == 0) {
       // every MMA issued above has completed once this commit arrives
       mma_commit(mma_done);
       mbar_wait_bounded(mma_done, 0, nullptr);
@@ -428,124 +554,132 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
     const int quarter = warp & 3;        // TMEM lanes 32*quarter .. +31
     const int row = quarter * 32 + lane;  // query row within the tile
     const uint32_t lane_base = tbase + ((uint32_t)(quarter * 32) << 16);
-    const bool valid_row = row < rows_valid;
-    const int pos = pos0 + row;
-    float m = -INFINITY, l = 0.f;
+    int64_t g = 0;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      const int s = j & 1;
-      if (ok && !mbar_wait_bounded(&s_full[s], (uint32_t)((j >> 1) & 1), p.err)) ok = false;
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok || *abort_flag) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t s_col = lane_base + (s ? kColS1 : kColS0);
-      uint32_t r0[32], r1[32];
-      tmem_ld32(s_col, r0);
-      tmem_ld32(s_col + 32, r1);
-      tmem_wait_ld();
-      const int key0 = j * kN;
-      // key c of this tile is visible iff key0 + c <= pos (then also < ctx). Tiles that
-      // every row of the warp sees whole (all but the diagonal ones) skip the masks.
-      const int nvis = valid_row ? min(kN, pos - key0 + 1) : 0;
-      const bool whole = __all_sync(0xffffffffu, nvis == kN);
-      float mx = whole ? row_max64<false>(r0, r1, nvis) : row_max64<true>(r0, r1, nvis);
-      mx = mx * p.scale_log2;  // scale_log2 > 0 keeps the arg-max
-      bool rescale = false;
-      float alpha = 1.f;
-      if (mx > -INFINITY) {
-        if (m == -INFINITY) {
-          m = mx;
-        } else if (mx > m + kRescaleThreshold) {
-          alpha = fast_exp2(m - mx);
-          m = mx;
-          rescale = true;
-        }
-      }
-      // Rows that move their reference max fix O once PV(j-1) has landed.
-      if (__any_sync(0xffffffffu, rescale)) {
-        if (!mbar_wait_bounded(&o_done[(j - 1) & 1], (uint32_t)(((j - 1) >> 1) & 1), p.err)) ok = false;
+    for (int i = 0; ok; ++i) {
+      ItemInfo it;
+      if (!take_item(i, it)) break;
+      if (it.n_kv == 0) continue;
+      const bool valid_row = row < it.rows_valid;
+      const int pos = it.pos0 + row;
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < it.n_kv; ++j, ++g) {
+        const int s = (int)(g & 1);
+        if (ok && !mbar_wait_bounded(&s_full[s], (uint32_t)((g >> 1) & 1), p.err)) ok = false;
         ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
+        if (!ok || *abort_flag) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
+        const uint32_t s_col = lane_base + (s ? kColS1 : kColS0);
+        uint32_t r0[32], r1[32];
+        tmem_ld32(s_col, r0);
+        tmem_ld32(s_col + 32, r1);
+        tmem_wait_ld();
+        const int key0 = j * kN;
+        // key c of this tile is visible iff key0 + c <= pos (then also < ctx). Tiles that
+        // every row of the warp sees whole (all but the diagonal ones) skip the masks.
+        const int nvis = valid_row ? min(kN, pos - key0 + 1) : 0;
+        const bool whole = __all_sync(0xffffffffu, nvis == kN);
+        float mx = whole ? row_max64<false>(r0, r1, nvis) : row_max64<true>(r0, r1, nvis);
+        mx = mx * p.scale_log2;  // scale_log2 > 0 keeps the arg-max
+        bool rescale = false;
+        float alpha = 1.f;
+        if (mx > -INFINITY) {
+          if (m == -INFINITY) {
+            m = mx;
+          } else if (mx > m + kRescaleThreshold) {
+            alpha = fast_exp2(m - mx);
+            m = mx;
+            rescale = true;
+          }
+        }
+        // Rows that move their reference max fix O once PV of the previous tile has landed.
+        if (__any_sync(0xffffffffu, rescale)) {
+          if (!mbar_wait_bounded(&o_done[(g - 1) & 1], (uint32_t)(((g - 1) >> 1) & 1), p.err)) ok = false;
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          tc_fence_after();
+          for (int c0 = 0; c0 < kD; c0 += 32) {
+            uint32_t o[32];
+            tmem_ld32(lane_base + kColO + c0, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+            tmem_st32(lane_base + kColO + c0, o);
+          }
+          tmem_wait_st();
+          l *= alpha;
+        }
+        uint32_t pk[32];
+        const float rs = whole ? row_exp64<T, false>(r0, r1, nvis, p.scale_log2, m, pk)
+                               : row_exp64<T, true>(r0, r1, nvis, p.scale_log2, m, pk);
+        l += rs;
+        tmem_st32(s_col, pk);
+        tmem_wait_st();
+        // Keys past the context (the last KV tile's tail) may hold NaN/Inf in the pool;
+        // P is 0 there but 0 * NaN is not: zero those V rows before the PV MMA reads them.
+        const int tail0 = it.ctx - key0;  // first row of this tile past the context
+        if (j == it.n_kv - 1 && tail0 < kN) {
+          if (!mbar_wait_bounded(&v_full[s], (uint32_t)((g >> 1) & 1), p.err)) ok = false;
+          uint8_t* vt = smem + kOffV + s * kKVBytes;
+          const int zrows = kN - max(tail0, 0);
+          for (int e = threadIdx.x - 64; e < 2 * zrows * 8; e += 128) {
+            const int c = e / (zrows * 8);         // d chunk
+            const int rem = e - c * zrows * 8;
+            const int r = max(tail0, 0) + rem / 8;  // token row
+            const int q16 = rem % 8;                // 16-byte piece of the 128-byte line
+            reinterpret_cast<uint4*>(vt + c * (kN * 128) + r * 128)[q16] = make_uint4(0, 0, 0, 0);
+          }
+          fence_proxy_async_smem();
+        }
+        tc_fence_before();
+        mbar_arrive(&p_full[s]);
+      }
+      // ---- epilogue: O / l -> out (the next item's first PV waits for this warp's arrival
+      // on its first P, which comes after these reads)
+      if (ok) {
+        const int64_t gl = g - 1;
+        if (!mbar_wait_bounded(&o_done[gl & 1], (uint32_t)((gl >> 1) & 1), p.err)) ok = false;
+        ok = __all_sync(0xffffffffu, ok);
+      }
+      if (ok) {
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        T* orow = reinterpret_cast<T*>(p.out) + (int64_t)(it.q0 + it.qt * kM + row) * p.o_tok +
+                  (int64_t)it.qh * p.o_head;
         for (int c0 = 0; c0 < kD; c0 += 32) {
           uint32_t o[32];
           tmem_ld32(lane_base + kColO + c0, o);
           tmem_wait_ld();
+          if (valid_row) {
+            uint32_t pk[16];
 #pragma unroll
-          for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-          tmem_st32(lane_base + kColO + c0, o);
-        }
-        tmem_wait_st();
-        l *= alpha;
-      }
-      uint32_t pk[32];
-      const float rs = whole ? row_exp64<T, false>(r0, r1, nvis, p.scale_log2, m, pk)
-                             : row_exp64<T, true>(r0, r1, nvis, p.scale_log2, m, pk);
-      l += rs;
-      tmem_st32(s_col, pk);
-      tmem_wait_st();
-      // Keys past the context (the last KV tile's tail) may hold NaN/Inf in the pool;
-      // P is 0 there but 0 * NaN is not: zero those V rows before the PV MMA reads them.
-      const int tail0 = ctx - key0;  // first row of this tile past the context
-      if (j == n_kv - 1 && tail0 < kN) {
-        if (!mbar_wait_bounded(&v_full[s], (uint32_t)((j >> 1) & 1), p.err)) ok = false;
-        uint8_t* vt = smem + kOffV + s * kKVBytes;
-        const int zrows = kN - max(tail0, 0);
-        for (int e = threadIdx.x - 64; e < 2 * zrows * 8; e += 128) {
-          const int c = e / (zrows * 8);         // d chunk
-          const int rem = e - c * zrows * 8;
-          const int r = max(tail0, 0) + rem / 8;  // token row
-          const int q16 = rem % 8;                // 16-byte piece of the 128-byte line
-          reinterpret_cast<uint4*>(vt + c * (kN * 128) + r * 128)[q16] = make_uint4(0, 0, 0, 0);
-        }
-        fence_proxy_async_smem();
-      }
-      tc_fence_before();
-      mbar_arrive(&p_full[s]);
-    }
-    // ---- epilogue: O / l -> out
-    if (ok && n_kv > 0) {
-      const int jl = n_kv - 1;
-      if (!mbar_wait_bounded(&o_done[jl & 1], (uint32_t)((jl >> 1) & 1), p.err)) ok = false;
-      ok = __all_sync(0xffffffffu, ok);
-    }
-    if (ok && n_kv > 0) {
-      tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      T* orow = reinterpret_cast<T*>(p.out) + (int64_t)(q0 + qt * kM + row) * p.o_tok +
-                (int64_t)qh * p.o_head;
-      for (int c0 = 0; c0 < kD; c0 += 32) {
-        uint32_t o[32];
-        tmem_ld32(lane_base + kColO + c0, o);
-        tmem_wait_ld();
-        if (valid_row) {
-          uint32_t pk[16];
+            for (int c = 0; c < 16; ++c)
+              pk[c] = pack2<T>(__uint_as_float(o[2 * c]) * inv, __uint_as_float(o[2 * c + 1]) * inv);
 #pragma unroll
-          for (int c = 0; c < 16; ++c)
-            pk[c] = pack2<T>(__uint_as_float(o[2 * c]) * inv, __uint_as_float(o[2 * c + 1]) * inv);
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            reinterpret_cast<uint4*>(orow + c0)[c] = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+            for (int c = 0; c < 4; ++c)
+              reinterpret_cast<uint4*>(orow + c0)[c] = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+          }
         }
+        tc_fence_before();
       }
+      if (!ok) *abort_flag = 1;
     }
-    if (!ok) *abort_flag = 1;
   }
 
   // ---- teardown: every TMA and MMA of this CTA has finished before TMEM is freed
+  __syncthreads();
   if (warp == 0 && lane == 0) {
-    // Q always lands before the CTA leaves; after an abort, so do the last two K/V tiles
-    // the producer issued.
-    mbar_wait_bounded(q_full, 0, nullptr);
-    if (*abort_flag) {
-      const int last = misc[2];
-      for (int j = max(0, last - 1); j <= last; ++j) {
-        mbar_wait_bounded(&k_full[j & 1], (uint32_t)((j >> 1) & 1), nullptr);
-        mbar_wait_bounded(&v_full[j & 1], (uint32_t)((j >> 1) & 1), nullptr);
-      }
+    // Loads this CTA issued land before it leaves: the last Q tile, and the last two K/V
+    // tiles (at most two are ever in flight).
+    const int nq_issued = misc[1];
+    if (nq_issued > 0) mbar_wait_bounded(q_full, (uint32_t)((nq_issued - 1) & 1), nullptr);
+    const int g_issued = misc[2];
+    for (int gg = max(0, g_issued - 2); gg < g_issued; ++gg) {
+      mbar_wait_bounded(&k_full[gg & 1], (uint32_t)((gg >> 1) & 1), nullptr);
+      mbar_wait_bounded(&v_full[gg & 1], (uint32_t)((gg >> 1) & 1), nullptr);
     }
   }
   tc_fence_before();
@@ -554,7 +688,18 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
   if (warp == 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase),
                  "r"(kTmemCols));
+  // The last CTA to finish re-zeroes the counters (every claim has been made by then).
+  if (threadIdx.x == 0 && atomicAdd(p.ctr + 1, 1) == (int)gridDim.x - 1) {
+    p.ctr[0] = 0;
+    p.ctr[1] = 0;
+    __threadfence();
+  }
 }
+
+// Claim counters of prefill launches. A launch takes the next of these slots (round robin)
+// and leaves it zeroed, so up to 64 launches can be in flight on a device at once.
+constexpr int kCounterSlots = 64;
+__device__ int32_t g_prefill_counters[kCounterSlots][2];
 
 }  // namespace
 
@@ -609,16 +754,69 @@ int b2p_prefill_tc(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
   p.o_tok = out_tok_stride;
   p.o_head = out_head_stride;
   p.err = err_flag;
+  p.hq = num_q_heads;
+  {
+    static void* base[64] = {nullptr};
+    static std::mutex mu;
+    static std::atomic<uint32_t> next_slot{0};
+    int dev = 0;
+    cudaError_t ce = cudaGetDevice(&dev);
+    if (ce != cudaSuccess) return b2p_host::record_error(ce);
+    if (dev < 0 || dev >= 64) return B2P_EUNSUPPORTED;
+    void* addr = nullptr;
+    {
+      std::lock_guard<std::mutex> lock(mu);
+      if (base[dev] == nullptr) {
+        ce = cudaGetSymbolAddress(&base[dev], g_prefill_counters);
+        if (ce != cudaSuccess) return b2p_host::record_error(ce);
+      }
+      addr = base[dev];
+    }
+    const uint32_t slot = next_slot.fetch_add(1) % kCounterSlots;
+    p.ctr = static_cast<int32_t*>(addr) + 2 * slot;
+  }
   const void* fn = dtype == B2P_BF16
                        ? reinterpret_cast<const void*>(&paged_prefill_tc<__nv_bfloat16>)
                        : reinterpret_cast<const void*>(&paged_prefill_tc<__half>);
   const int smem = kSmemBytes + 1024;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return b2p_host::record_error(e);
-  // Upper bound on the number of 128-row tiles: sum(ceil(q_len / 128)) <= seqs + rows / 128.
-  const int64_t tiles = (int64_t)num_seqs + total_q / kM + 1;
-  if (tiles > 0x7fffffffLL) return B2P_EUNSUPPORTED;
-  dim3 grid((unsigned)tiles, (unsigned)num_q_heads);
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return b2p_host::record_error(e);
+  // Persistent: every resident CTA walks the work items (tile-items x query heads). The
+  // residency comes from the SM's own limits (shared memory with the per-CTA reservation,
+  // the register file, tensor memory: two CTAs' 256 columns fill it), computed once per
+  // device. cudaOccupancyMaxActiveBlocksPerMultiprocessor answers 1 for this kernel on
+  // B200 although two CTAs run side by side (measured: 296 CTAs started within 1 us on
+  // 148 SMs, at TMEM columns 0 and 256), and a grid of one CTA per SM ran 1.6x slower.
+  static int resident[64] = {0};
+  int dev = 0;
+  e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return b2p_host::record_error(e);
+  if (dev < 0 || dev >= 64) return B2P_EUNSUPPORTED;
+  if (resident[dev] == 0) {
+    cudaFuncAttributes fa;
+    int smem_sm = 0, reserved = 0, regs_sm = 0;
+    if ((e = cudaFuncGetAttributes(&fa, fn)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor,
+                                    dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev)) !=
+            cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev)) !=
+            cudaSuccess)
+      return b2p_host::record_error(e);
+    // registers are handed out per warp in 256-register units
+    const int warp_regs = (fa.numRegs * 32 + 255) / 256 * 256;
+    const int by_regs = regs_sm / (warp_regs * (kThreads / 32));
+    const int by_smem = smem_sm / (smem + (int)fa.sharedSizeBytes + reserved);
+    int n = by_regs < by_smem ? by_regs : by_smem;
+    if (n > 2) n = 2;
+    resident[dev] = n;
+  }
+  const int per_sm = resident[dev];
+  if (per_sm <= 0) return B2P_EUNSUPPORTED;
+  dim3 grid((unsigned)(b2p_host::sm_count() * per_sm));
   void* args[] = {&qmap, &kmap, &vmap, &p};
   e = cudaLaunchKernel(fn, grid, dim3(kThreads), args, (size_t)smem,
                        static_cast<cudaStream_t>(stream));
