@@ -65,9 +65,9 @@ constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kQBytes;       // 2 stages
 constexpr int kOffV = kOffK + 2 * kKVBytes;  // 2 stages
 constexpr int kOffBar = kOffV + 2 * kKVBytes;
-constexpr int kNumBars = 1 + 2 * 6 + 1 + 1 + 4;  // q_full, k_full[2], v_full[2], kv_empty[2],
-                                                // s_full[2], p_full[2], o_done[2], mma_done,
-                                                // q_empty, item_full[2], item_empty[2]
+constexpr int kNumBars = 1 + 2 * 7 + 1 + 1 + 4;  // q_full, k_full[2], v_full[2], k_empty[2],
+                                                // s_full[2], p_full[2], o_done[2], v_empty[2],
+                                                // mma_done, q_empty, item_full[2], item_empty[2]
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kOffItems = kOffMisc + 64;
 constexpr int kSmemBytes = kOffItems + 2 * 48;
@@ -280,14 +280,15 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = bars + 3;
-  uint64_t* kv_empty = bars + 5;
+  uint64_t* k_empty = bars + 5;
   uint64_t* s_full = bars + 7;
   uint64_t* p_full = bars + 9;
   uint64_t* o_done = bars + 11;
-  uint64_t* mma_done = bars + 13;
-  uint64_t* q_empty = bars + 14;
-  uint64_t* item_full = bars + 15;
-  uint64_t* item_empty = bars + 17;
+  uint64_t* v_empty = bars + 13;
+  uint64_t* mma_done = bars + 15;
+  uint64_t* q_empty = bars + 16;
+  uint64_t* item_full = bars + 17;
+  uint64_t* item_empty = bars + 19;
   int32_t* misc = reinterpret_cast<int32_t*>(smem + kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 5);
@@ -299,12 +300,13 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
 
   if (warp == 0 && lane == 0) {
     *abort_flag = 0;
-    misc[0] = misc[1] = misc[2] = 0;
+    misc[0] = misc[1] = misc[2] = misc[3] = 0;
     mbar_init(q_full, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&p_full[s], kM);
       mbar_init(&o_done[s], 1);
@@ -366,6 +368,24 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
     int64_t g = 0;  // K/V tiles issued by this CTA (stage = g & 1)
     int nq = 0;     // Q tiles issued
     bool aborted = false;
+    int64_t v_slots[4] = {0, 0, 0, 0};  // slots of the V tile not yet issued (lane 0)
+    // V(gv) into stage gv & 1 once PV(gv - 2) has read that stage (lane 0 only).
+    auto issue_v = [&](int64_t gv, const int64_t (&sl)[4], int kvh_) -> bool {
+      const int sv = (int)(gv & 1);
+      if (gv >= 2 && !mbar_wait_bounded(&v_empty[sv], (uint32_t)(((gv >> 1) - 1) & 1), p.err))
+        return false;
+      if (*abort_flag) return false;
+      uint8_t* vdst = smem + kOffV + sv * kKVBytes;
+      mbar_arrive_expect_tx(&v_full[sv], kKVBytes);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+          tma_load_5d(vdst + c * (kN * 128) + u * (kSub * 128), &vmap, &v_full[sv], 0, c, kvh_,
+                      (int)sl[u], p.layer);
+      misc[3] = (int)(gv + 1);  // V tiles issued
+      return true;
+    };
     // Claims run one item ahead: the next item's claim is in flight while this one's tiles
     // are issued.
     int32_t claim = 0;
@@ -446,14 +466,14 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
 #pragma unroll
         for (int u = 0; u < 4; ++u) slots[u] = __shfl_sync(0xffffffffu, my_slot, j * 4 - win + u);
         if (lane == 0) {
-          if (g >= 2 && !mbar_wait_bounded(&kv_empty[s], (uint32_t)(((g >> 1) - 1) & 1), p.err)) {
-            *abort_flag = 1;
+          // K(g) first, then V(g - 1): K stages free up as soon as their QK^T MMAs finish, so
+          // the next K load is in flight while the softmax of the current tile runs.
+          if (g >= 2 && !mbar_wait_bounded(&k_empty[s], (uint32_t)(((g >> 1) - 1) & 1), p.err)) {
             aborted = true;
           } else if (*abort_flag) {
             aborted = true;
           } else {
             uint8_t* kdst = smem + kOffK + s * kKVBytes;
-            uint8_t* vdst = smem + kOffV + s * kKVBytes;
             mbar_arrive_expect_tx(&k_full[s], kKVBytes);
 #pragma unroll
             for (int u = 0; u < 4; ++u)
@@ -461,18 +481,21 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
               for (int c = 0; c < 2; ++c)
                 tma_load_5d(kdst + c * (kN * 128) + u * (kSub * 128), &kmap, &k_full[s], 0, c,
                             kvh, (int)slots[u], p.layer);
-            mbar_arrive_expect_tx(&v_full[s], kKVBytes);
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-#pragma unroll
-              for (int c = 0; c < 2; ++c)
-                tma_load_5d(vdst + c * (kN * 128) + u * (kSub * 128), &vmap, &v_full[s], 0, c,
-                            kvh, (int)slots[u], p.layer);
-            misc[2] = (int)(g + 1);  // K/V tiles issued
+            misc[2] = (int)(g + 1);  // K tiles issued
+            if (j > 0 && !issue_v(g - 1, v_slots, kvh)) aborted = true;
           }
+          if (aborted) *abort_flag = 1;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) v_slots[u] = slots[u];
         }
         aborted = __shfl_sync(0xffffffffu, aborted ? 1 : 0, 0) != 0;
       }
+      // the item's last V tile
+      if (lane == 0 && !aborted && !issue_v(g - 1, v_slots, kvh)) {
+        *abort_flag = 1;
+        aborted = true;
+      }
+      aborted = __shfl_sync(0xffffffffu, aborted ? 1 : 0, 0) != 0;
       if (aborted) break;
     }
     if (aborted && lane == 0) {  // the consumers learn it from the flag or their waits
@@ -502,6 +525,7 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
             mma_ss(d, da, db, id_qk, kk > 0 ? 1u : 0u);
           }
           mma_commit(&s_full[s]);
+          mma_commit(&k_empty[s]);  // K stage s is free once these MMAs have read it
         };
         // S buffer g & 1 held P of tile g - 2: PV(g - 2) must be done reading it.
         auto s_free = [&](int64_t gg) -> bool {
@@ -535,7 +559,7 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
             const uint64_t db = smem_desc_sw128(v_addr + kk * (16 * 128), kN * 128, 1024);
             mma_ts(tbase + kColO, p_tmem + kk * 8, db, id_pv, (j > 0 || kk > 0) ? 1u : 0u);
           }
-          mma_commit(&kv_empty[s]);
+          mma_commit(&v_empty[s]);
           mma_commit(&o_done[s]);
         }
         if (!ok) *abort_flag = 1;
@@ -676,11 +700,12 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
     // tiles (at most two are ever in flight).
     const int nq_issued = misc[1];
     if (nq_issued > 0) mbar_wait_bounded(q_full, (uint32_t)((nq_issued - 1) & 1), nullptr);
-    const int g_issued = misc[2];
-    for (int gg = max(0, g_issued - 2); gg < g_issued; ++gg) {
+    const int k_issued = misc[2];
+    for (int gg = max(0, k_issued - 2); gg < k_issued; ++gg)
       mbar_wait_bounded(&k_full[gg & 1], (uint32_t)((gg >> 1) & 1), nullptr);
+    const int v_issued = misc[3];
+    for (int gg = max(0, v_issued - 2); gg < v_issued; ++gg)
       mbar_wait_bounded(&v_full[gg & 1], (uint32_t)((gg >> 1) & 1), nullptr);
-    }
   }
   tc_fence_before();
   __syncthreads();
