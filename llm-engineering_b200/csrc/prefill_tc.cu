@@ -3,26 +3,32 @@
 // Reference path replaced (PREFILL executions): HFBatchedPagedCache.update gathers every
 // history (serving/engine/hf_batched_paged_cache.py:52-148), build_attention_mask adds a
 // dense tril block per prefill (serving/engine/attention_mask.py:37-45) and HF SDPA runs
-// over all packed keys (transformers/integrations/sdpa_attention.py:40-104). Here each CTA
-// computes one tile of 128 query rows of one (sequence, query head) against the sequence's
-// keys read in place from the paged pool:
+// over all packed keys (transformers/integrations/sdpa_attention.py:40-104). Here a work
+// item is one tile of 128 query rows of one sequence for two query heads of the same GQA
+// group (A and B), attended against the sequence's keys read in place from the paged pool:
 //
 //   S = Q K^T   tcgen05.mma kind::f16, A = Q (smem, K-major), B = K tile (smem, K-major),
-//               D = S in tensor memory (fp32, 128 lanes x 64 columns, two buffers)
+//               D = S in tensor memory (fp32, 128 lanes x 128 columns, one per head)
 //   P = softmax rows of S, one thread per query row (tcgen05.ld -> fp32 -> exp2), written
-//       back as bf16/f16 over its own S buffer (tcgen05.st)
+//       back as bf16/f16 over the second half of its own S columns (tcgen05.st)
 //   O += P V    tcgen05.mma with A = P from tensor memory, B = V tile (smem, MN-major),
-//               D = O in tensor memory (fp32, 128 x head_dim)
+//               D = O in tensor memory (fp32, 128 x head_dim, one per head)
 //
-// K/V tiles of 64 tokens are assembled from four 16-slot pool sub-blocks (TMA tile loads,
-// 128-byte swizzle, no multicast) into a two-stage ring. A query row j of sequence i sits
-// at position ctx_i - q_len_i + j and sees keys 0..position (whole-history prefill when
-// q_len == ctx, chunked prefill otherwise). The running max is only moved (and O rescaled)
-// when a row's max grows by more than 2^8, so exp2 values stay below 256 and the O
-// correction is rare.
+// Tensor memory holds S_A, S_B, O_A, O_B (512 columns, one CTA per SM). The MMA warp
+// issues PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1), ..., so the softmax of one head runs
+// while the tensor cores work on the other head, and both heads read each K/V tile once.
+// K/V tiles of 128 tokens are assembled from eight 16-slot pool sub-blocks (TMA tile
+// loads, 128-byte swizzle, no multicast) into two-stage K and V rings. A query row j of
+// sequence i sits at position ctx_i - q_len_i + j and sees keys 0..position (whole-history
+// prefill when q_len == ctx, chunked prefill otherwise). The first KV tile of an item sets
+// each row's reference max; later tiles take exp2 against that reference in one pass (the
+// row sum flags the rare rows whose scores outgrow it by more than 2^8, which then move
+// the reference and rescale O, l and the P already stored). The softmax is bound by FP32
+// instruction issue, so the exponent arithmetic runs as packed f32x2 FMA/ADD.
 //
-// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = tensor-memory owner and MMA
-// issuer (one thread), warps 2..5 = softmax + epilogue (thread = TMEM lane = query row).
+// Warp roles (320 threads): warp 0 = TMA producer and work-item scheduler, warp 1 =
+// tensor-memory owner and MMA issuer (one thread), warps 2..5 = softmax + epilogue of head
+// A, warps 6..9 = the same for head B (thread = TMEM lane = query row).
 #include <atomic>
 #include <mutex>
 #include <type_traits>
@@ -34,10 +40,12 @@ namespace {
 using namespace b2p;
 
 constexpr int kM = 128;     // query rows per tile
-constexpr int kN = 64;      // keys per KV tile
+constexpr int kN = 128;     // keys per KV tile
 constexpr int kD = 128;     // head_dim handled by this kernel
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 constexpr int kSub = 16;
+constexpr int kSubPerTile = kN / kSub;
+constexpr int kConsumerWarps = 9;  // the MMA issuer and eight softmax warps
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct PrefillParams {
@@ -59,22 +67,30 @@ struct PrefillParams {
 };
 
 // Shared-memory plan (bytes from the 1024-aligned base).
-constexpr int kQBytes = 2 * kM * 128;        // 2 chunks x 128 rows x 128 B
-constexpr int kKVBytes = 2 * kN * 128;       // 2 chunks x 64 rows x 128 B
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kQBytes;       // 2 stages
+constexpr int kQBytes = 2 * kM * 128;        // one head: 2 chunks x 128 rows x 128 B
+constexpr int kKVBytes = 2 * kN * 128;       // 2 chunks x 128 rows x 128 B
+constexpr int kOffQ = 0;                     // heads A and B
+constexpr int kOffK = kOffQ + 2 * kQBytes;   // 2 stages
 constexpr int kOffV = kOffK + 2 * kKVBytes;  // 2 stages
 constexpr int kOffBar = kOffV + 2 * kKVBytes;
-constexpr int kNumBars = 1 + 2 * 7 + 1 + 1 + 4;  // q_full, k_full[2], v_full[2], k_empty[2],
-                                                // s_full[2], p_full[2], o_done[2], v_empty[2],
-                                                // mma_done, q_empty, item_full[2], item_empty[2]
+constexpr int kNumBars = 21;  // q_full, q_empty, k_full[2], k_empty[2], v_full[2], v_empty[2],
+                              // s_full[2], p_full[2], o_done[2] (by head), item_full[2],
+                              // item_empty[2], mma_done
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kOffItems = kOffMisc + 64;
-constexpr int kSmemBytes = kOffItems + 2 * 48;
+constexpr int kOffStage = (kOffItems + 2 * 48 + 127) / 128 * 128;  // epilogue: 8 warps x 32 rows x 64 B
+constexpr int kStageBytes = 32 * 64;
+constexpr int kSeqCache = 2048;
+constexpr int kRoundCache = 1024;
+constexpr int kOffSched = kOffStage + 8 * kStageBytes;  // scheduler tables
+constexpr int kSmemBytes = kOffSched + (kSeqCache + kRoundCache + 1) * 4;
 
-// TMEM columns: S buffers at 0 and 64, O at 128 (256 allocated).
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kColS0 = 0, kColS1 = 64, kColO = 128;
+// TMEM columns (512 allocated): S of head A at 0, of head B at 128, O_A at 256, O_B at
+// 384. P overwrites the second half of its S (columns +64 .. +127, two keys per column).
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColP = 64;
+__device__ __forceinline__ uint32_t col_s(int h) { return h ? 128u : 0u; }
+__device__ __forceinline__ uint32_t col_o(int h) { return h ? 384u : 256u; }
 
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   uint64_t d = 0;
@@ -151,6 +167,24 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32
           taddr),
       B2P_W32(v));
 }
+// 16 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+      "%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15]));
+}
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -170,55 +204,109 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* m
 
 __device__ __forceinline__ int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
+// Two fp32 values in one 64-bit register for the packed f32x2 FMA-pipe instructions.
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // Row max of a 64-key S tile (columns 0..31 in r0, 32..63 in r1), four independent
-// chains. kMasked: keys at or past `nvis` are ignored.
+// three-input max chains. kMasked: keys at or past `nvis` are ignored.
 template <bool kMasked>
 __device__ __forceinline__ float row_max64(const uint32_t (&r0)[32], const uint32_t (&r1)[32],
                                            int nvis) {
   float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
+  auto v = [&](const uint32_t (&r)[32], int base, int c) {
+    const float x = __uint_as_float(r[c]);
+    return (!kMasked || base + c < nvis) ? x : -INFINITY;
+  };
 #pragma unroll
-  for (int c = 0; c < 32; c += 2) {
-    const float x0 = __uint_as_float(r0[c]), x1 = __uint_as_float(r0[c + 1]);
-    const float x2 = __uint_as_float(r1[c]), x3 = __uint_as_float(r1[c + 1]);
-    a0 = fmaxf(a0, (!kMasked || c < nvis) ? x0 : -INFINITY);
-    a1 = fmaxf(a1, (!kMasked || c + 1 < nvis) ? x1 : -INFINITY);
-    a2 = fmaxf(a2, (!kMasked || 32 + c < nvis) ? x2 : -INFINITY);
-    a3 = fmaxf(a3, (!kMasked || 33 + c < nvis) ? x3 : -INFINITY);
+  for (int c = 0; c < 32; c += 4) {
+    a0 = fmax3(a0, v(r0, 0, c), v(r0, 0, c + 1));
+    a1 = fmax3(a1, v(r0, 0, c + 2), v(r0, 0, c + 3));
+    a2 = fmax3(a2, v(r1, 32, c), v(r1, 32, c + 1));
+    a3 = fmax3(a3, v(r1, 32, c + 2), v(r1, 32, c + 3));
   }
   return fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
 }
 
 // P = exp2(S * scale_log2 - m) of a 64-key row, packed in pairs for tcgen05.st; returns
-// the row sum. kMasked: keys at or past `nvis` get 0.
+// the row sum. kMasked: keys at or past `nvis` get 0. (Moving part of the exp2 work to the FMA pipe
+// with a polynomial was measured slower here: the softmax is bound by instruction issue
+// and latency, not by MUFU throughput.)
 template <typename T, bool kMasked>
 __device__ __forceinline__ float row_exp64(const uint32_t (&r0)[32], const uint32_t (&r1)[32],
                                            int nvis, float scale_log2, float m,
                                            uint32_t (&pk)[32]) {
-  float s0 = 0.f, s1 = 0.f;
+  const uint64_t sc = f2pack(scale_log2, scale_log2);
+  const uint64_t nm = f2pack(-m, -m);
+  uint64_t acc0 = f2pack(0.f, 0.f), acc1 = f2pack(0.f, 0.f);
 #pragma unroll
-  for (int c = 0; c < 16; ++c) {  // tokens 0..31 from r0, 32..63 from r1
-    const float e0 = (!kMasked || 2 * c < nvis) ? fast_exp2(__uint_as_float(r0[2 * c]) * scale_log2 - m) : 0.f;
-    const float e1 = (!kMasked || 2 * c + 1 < nvis) ? fast_exp2(__uint_as_float(r0[2 * c + 1]) * scale_log2 - m) : 0.f;
-    const float e2 = (!kMasked || 32 + 2 * c < nvis) ? fast_exp2(__uint_as_float(r1[2 * c]) * scale_log2 - m) : 0.f;
-    const float e3 = (!kMasked || 33 + 2 * c < nvis) ? fast_exp2(__uint_as_float(r1[2 * c + 1]) * scale_log2 - m) : 0.f;
-    s0 += e0 + e1;
-    s1 += e2 + e3;
-    pk[c] = pack2<T>(e0, e1);
-    pk[16 + c] = pack2<T>(e2, e3);
+  for (int q = 0; q < 32; ++q) {  // pair q: keys 2q, 2q+1 (r0 for q < 16, r1 after)
+    const uint32_t* r = q < 16 ? r0 : r1;
+    const int c = (q & 15) * 2;
+    const uint64_t x = ffma2(f2pack(__uint_as_float(r[c]), __uint_as_float(r[c + 1])), sc, nm);
+    float x0, x1, e0, e1;
+    f2unpack(x, x0, x1);
+    e0 = fast_exp2(x0);
+    e1 = fast_exp2(x1);
+    if (kMasked) {
+      e0 = 2 * q < nvis ? e0 : 0.f;
+      e1 = 2 * q + 1 < nvis ? e1 : 0.f;
+    }
+    if (q & 1) acc1 = fadd2(acc1, f2pack(e0, e1)); else acc0 = fadd2(acc0, f2pack(e0, e1));
+    pk[q] = pack2<T>(e0, e1);
   }
-  return s0 + s1;
+  float s0, s1, s2, s3;
+  f2unpack(acc0, s0, s1);
+  f2unpack(acc1, s2, s3);
+  return (s0 + s1) + (s2 + s3);
+}
+
+// P of a row half as stored (two 16-bit values per column) times a, in place.
+template <typename T>
+__device__ __forceinline__ uint32_t scale_pair(uint32_t v, float a);
+template <>
+__device__ __forceinline__ uint32_t scale_pair<__nv_bfloat16>(uint32_t v, float a) {
+  const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v));
+  return pack2<__nv_bfloat16>(f.x * a, f.y * a);
+}
+template <>
+__device__ __forceinline__ uint32_t scale_pair<__half>(uint32_t v, float a) {
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&v));
+  return pack2<__half>(f.x * a, f.y * a);
 }
 
 // Work items. Sequence s has ntiles(s) = ceil(q_len_s / 128) query tiles; tile-items are
 // ordered round by round from the end: round r holds tile ntiles(s) - 1 - r of every
 // sequence with more than r tiles, sequences in index order. A sequence's later tiles see
 // more keys, so the order runs close to longest first (LPT) whatever the prompt mix. Work
-// item k is tile-item k / HQ for query head k % HQ: the query heads of one tile are
-// neighbours, so the heads of a GQA group, which read the same K/V tiles, run together and
-// share them through L2.
+// item k is tile-item k / (HKV * pairs) for head pair k % (HKV * pairs): the query heads of
+// a GQA group go two by two (the last one alone when the group is odd), and the pairs of
+// one tile are neighbours, so the whole group reads the same K/V tiles close together.
 struct ItemInfo {
   int seq;  // -1: no more work for this CTA
-  int qt, qh, q0, qlen, ctx, rows_valid, pos0, n_kv, pad[3];
+  int qt, kvh, qh_a, qh_b;  // qh_b = -1: head A only
+  int q0, qlen, ctx, rows_valid, pos0, n_kv, pad;
 };
 
 __device__ __forceinline__ int ntiles_of(const PrefillParams& p, int s) {
@@ -232,25 +320,82 @@ __device__ __forceinline__ int64_t warp_sum64(int64_t v) {
   return v;
 }
 
+// Scheduler tables in shared memory, built once per CTA by the producer warp: the tile
+// counts of the first kSeqCache sequences, and the tile-items before each round when the
+// longest sequence has at most kRoundCache tiles. Past either size the scheduler reads
+// cu_seqlens directly (same results, more global round trips per item).
+struct SchedTables {
+  int32_t* nt;      // [kSeqCache]
+  int32_t* before;  // [kRoundCache + 1]
+  bool rounds;      // `before` holds rounds 0..maxnt
+};
+
+__device__ __forceinline__ int nt_of(const PrefillParams& p, const SchedTables& st, int s) {
+  return s < kSeqCache ? st.nt[s] : ntiles_of(p, s);
+}
+
 // Tile-items in rounds before r: sum over sequences of min(ntiles, r). One warp.
-__device__ int64_t items_before_round(const PrefillParams& p, int r, int lane) {
+__device__ __forceinline__ int64_t items_before_round(const PrefillParams& p, const SchedTables& st, int r,
+                                      int lane) {
+  if (st.rounds) return st.before[r];
   int64_t acc = 0;
-  for (int s = lane; s < p.num_seqs; s += 32) acc += min(ntiles_of(p, s), r);
+  for (int s = lane; s < p.num_seqs; s += 32) acc += min(nt_of(p, st, s), r);
   return warp_sum64(acc);
 }
 
+// Fills the tables and returns the total tile-items (all lanes); maxnt gets the longest
+// sequence's tile count. One warp.
+__device__ __forceinline__ int64_t build_sched_tables(const PrefillParams& p, SchedTables& st, int lane,
+                                      int& maxnt) {
+  int64_t total = 0;
+  maxnt = 0;
+  for (int s = lane; s < p.num_seqs; s += 32) {
+    const int nt = ntiles_of(p, s);
+    if (s < kSeqCache) st.nt[s] = nt;
+    total += nt;
+    maxnt = max(maxnt, nt);
+  }
+  total = warp_sum64(total);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) maxnt = max(maxnt, __shfl_xor_sync(0xffffffffu, maxnt, o));
+  st.rounds = maxnt <= kRoundCache;
+  if (st.rounds) {
+    for (int r = lane; r <= maxnt; r += 32) st.before[r] = 0;
+    __syncwarp();
+    for (int s = lane; s < p.num_seqs; s += 32) atomicAdd(&st.before[nt_of(p, st, s)], 1);
+    __syncwarp();
+    if (lane == 0) {
+      // histogram of tile counts -> sequences with more than r tiles -> items before r
+      int suffix = 0;
+      for (int r = maxnt; r >= 0; --r) {
+        const int h = st.before[r];
+        st.before[r] = suffix;
+        suffix += h;
+      }
+      int acc = 0;
+      for (int r = 0; r <= maxnt; ++r) {
+        const int c = st.before[r];
+        st.before[r] = acc;
+        acc += c;
+      }
+    }
+    __syncwarp();
+  }
+  return total;
+}
+
 // Tile-item t -> (sequence, query tile). One warp; all lanes get the result.
-__device__ bool decode_tile_item(const PrefillParams& p, int64_t t, int maxnt, int lane,
-                                 int& seq, int& tile) {
+__device__ __forceinline__ bool decode_tile_item(const PrefillParams& p, const SchedTables& st, int64_t t,
+                                 int maxnt, int lane, int& seq, int& tile) {
   int lo = 0, hi = maxnt - 1;  // largest r with items_before_round(r) <= t
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
-    if (items_before_round(p, mid, lane) <= t) lo = mid; else hi = mid - 1;
+    if (items_before_round(p, st, mid, lane) <= t) lo = mid; else hi = mid - 1;
   }
-  int64_t i = t - items_before_round(p, lo, lane);
+  int64_t i = t - items_before_round(p, st, lo, lane);
   for (int base = 0; base < p.num_seqs; base += 32) {
     const int s = base + lane;
-    const int nt = s < p.num_seqs ? ntiles_of(p, s) : 0;
+    const int nt = s < p.num_seqs ? nt_of(p, st, s) : 0;
     const unsigned m = __ballot_sync(0xffffffffu, nt > lo);
     const int c = __popc(m);
     if (i < c) {
@@ -264,12 +409,12 @@ __device__ bool decode_tile_item(const PrefillParams& p, int64_t t, int maxnt, i
   return false;
 }
 
-// Persistent CTAs (two per SM) claim work items in the order above from an atomic counter
-// (dynamic, so faster SMs take more items and the short items come last). Tensor memory, barriers and descriptors are set up once; the stage, S-buffer and
-// item counters run on across items, so the next item's Q and first K/V tiles load while
-// the current item finishes, and its first QK^T MMAs run during the current epilogue.
+// Persistent CTAs (one per SM) claim work items in the order above from an atomic counter
+// (dynamic, so faster SMs take more items and the short items come last). Tensor memory,
+// barriers and descriptors are set up once; the stage and per-head counters run on across
+// items, so the next item's Q and first K/V tiles load while the current item finishes.
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_constant__ CUtensorMap qmap,
+__global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_constant__ CUtensorMap qmap,
                                                                 const __grid_constant__ CUtensorMap kmap,
                                                                 const __grid_constant__ CUtensorMap vmap,
                                                                 const PrefillParams p) {
@@ -278,17 +423,17 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* v_full = bars + 3;
-  uint64_t* k_empty = bars + 5;
-  uint64_t* s_full = bars + 7;
-  uint64_t* p_full = bars + 9;
-  uint64_t* o_done = bars + 11;
-  uint64_t* v_empty = bars + 13;
-  uint64_t* mma_done = bars + 15;
-  uint64_t* q_empty = bars + 16;
-  uint64_t* item_full = bars + 17;
-  uint64_t* item_empty = bars + 19;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* k_full = bars + 2;       // by stage
+  uint64_t* k_empty = bars + 4;
+  uint64_t* v_full = bars + 6;
+  uint64_t* v_empty = bars + 8;
+  uint64_t* s_full = bars + 10;      // by head (A, B)
+  uint64_t* p_full = bars + 12;
+  uint64_t* o_done = bars + 14;
+  uint64_t* item_full = bars + 16;   // by ring slot
+  uint64_t* item_empty = bars + 18;
+  uint64_t* mma_done = bars + 20;
   int32_t* misc = reinterpret_cast<int32_t*>(smem + kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 5);
@@ -302,22 +447,22 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
     *abort_flag = 0;
     misc[0] = misc[1] = misc[2] = misc[3] = 0;
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&k_full[s], 1);
-      mbar_init(&v_full[s], 1);
       mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&p_full[s], kM);
       mbar_init(&o_done[s], 1);
       mbar_init(&item_full[s], 1);
-      mbar_init(&item_empty[s], 5);  // the MMA issuer and the four softmax warps
+      mbar_init(&item_empty[s], kConsumerWarps);
     }
     mbar_init(mma_done, 1);
-    mbar_init(q_empty, 1);
     fence_mbar_init();
   }
-  if (warp == 1) {  // tensor memory for S0, S1, O
+  if (warp == 1) {  // tensor memory for S_A, S_B, O_A, O_B
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
                  "r"(kTmemCols));
@@ -347,17 +492,14 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
 
   if (warp == 0) {
     // ---------------------------------------------------------------- scheduler + producer
-    int64_t total = 0;
+    SchedTables st;
+    st.nt = reinterpret_cast<int32_t*>(smem + kOffSched);
+    st.before = st.nt + kSeqCache;
     int maxnt = 0;
-    for (int s = lane; s < p.num_seqs; s += 32) {
-      const int nt = ntiles_of(p, s);
-      total += nt;
-      maxnt = max(maxnt, nt);
-    }
-    total = warp_sum64(total);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) maxnt = max(maxnt, __shfl_xor_sync(0xffffffffu, maxnt, o));
-    const int64_t n_items = total * p.hq;
+    const int64_t total = build_sched_tables(p, st, lane, maxnt);
+    const int pairs = (p.group + 1) >> 1;
+    const int64_t per_tile = (int64_t)(p.hq / p.group) * pairs;
+    const int64_t n_items = total * per_tile;
     const int spb = p.block_size / kSub;
     const int64_t num_slots = p.num_blocks * p.block_size;
     if (lane == 0) {
@@ -366,11 +508,10 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
       tma_prefetch_desc(&vmap);
     }
     int64_t g = 0;  // K/V tiles issued by this CTA (stage = g & 1)
-    int nq = 0;     // Q tiles issued
+    int nq = 0;     // Q loads issued
     bool aborted = false;
-    int64_t v_slots[4] = {0, 0, 0, 0};  // slots of the V tile not yet issued (lane 0)
-    // V(gv) into stage gv & 1 once PV(gv - 2) has read that stage (lane 0 only).
-    auto issue_v = [&](int64_t gv, const int64_t (&sl)[4], int kvh_) -> bool {
+    // V(gv) into stage gv & 1 once PV of tile gv - 2 has read that stage (lane 0 only).
+    auto issue_v = [&](int64_t gv, const int32_t (&sl)[kSubPerTile], int kvh_) -> bool {
       const int sv = (int)(gv & 1);
       if (gv >= 2 && !mbar_wait_bounded(&v_empty[sv], (uint32_t)(((gv >> 1) - 1) & 1), p.err))
         return false;
@@ -378,11 +519,11 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
       uint8_t* vdst = smem + kOffV + sv * kKVBytes;
       mbar_arrive_expect_tx(&v_full[sv], kKVBytes);
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
+      for (int u = 0; u < kSubPerTile; ++u)
 #pragma unroll
         for (int c = 0; c < 2; ++c)
           tma_load_5d(vdst + c * (kN * 128) + u * (kSub * 128), &vmap, &v_full[sv], 0, c, kvh_,
-                      (int)sl[u], p.layer);
+                      sl[u], p.layer);
       misc[3] = (int)(gv + 1);  // V tiles issued
       return true;
     };
@@ -396,10 +537,14 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
       it.seq = -1;
       if (k < n_items && !aborted) {
         int seq = 0, tile = 0;
-        if (decode_tile_item(p, k / p.hq, maxnt, lane, seq, tile)) {
+        if (decode_tile_item(p, st, k / per_tile, maxnt, lane, seq, tile)) {
+          const int r = (int)(k % per_tile);
+          const int pr = r % pairs;
           it.seq = seq;
           it.qt = tile;
-          it.qh = (int)(k % p.hq);
+          it.kvh = r / pairs;
+          it.qh_a = it.kvh * p.group + 2 * pr;
+          it.qh_b = 2 * pr + 1 < p.group ? it.qh_a + 1 : -1;
           it.q0 = __ldg(p.cu_q + seq);
           it.qlen = __ldg(p.cu_q + seq + 1) - it.q0;
           it.ctx = __ldg(p.ctx + seq);
@@ -427,31 +572,33 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
       if (it.seq < 0 || aborted) break;
       if (lane == 0) claim = atomicAdd(p.ctr, 1);
       if (it.n_kv == 0) continue;
-      const int kvh = it.qh / p.group;
+      const int kvh = it.kvh;
       if (lane == 0) {
-        // The previous item's QK^T MMAs are done with the Q buffer before it is refilled.
+        // The previous item's QK^T MMAs are done with the Q buffers before they are refilled.
         if (nq >= 1 && !mbar_wait_bounded(q_empty, (uint32_t)((nq - 1) & 1), p.err)) {
           *abort_flag = 1;
           aborted = true;
         } else {
-          mbar_arrive_expect_tx(q_full, kQBytes);
-          for (int c = 0; c < 2; ++c)
-            tma_load_4d(smem + kOffQ + c * (kM * 128), &qmap, q_full, 0, c, it.qh,
-                        it.q0 + it.qt * kM);
-          misc[1] = nq + 1;  // Q tiles issued
+          const int nh = it.qh_b >= 0 ? 2 : 1;
+          mbar_arrive_expect_tx(q_full, nh * kQBytes);
+          for (int h = 0; h < nh; ++h)
+            for (int c = 0; c < 2; ++c)
+              tma_load_4d(smem + kOffQ + h * kQBytes + c * (kM * 128), &qmap, q_full, 0, c,
+                          h ? it.qh_b : it.qh_a, it.q0 + it.qt * kM);
+          misc[1] = nq + 1;  // Q loads issued
         }
       }
       aborted = __shfl_sync(0xffffffffu, aborted ? 1 : 0, 0) != 0;
       if (aborted) break;
       ++nq;
       const int32_t* bt = p.block_tables + (int64_t)it.seq * p.bt_stride;
-      // lane l holds the slot of sub-block (win + l); 8 KV tiles per window
+      // lane l holds the slot of sub-block (win + l); 4 KV tiles per window
       int win = -32;
-      int64_t my_slot = 0;
+      int32_t my_slot = 0;  // slot indices fit in int32 (checked on the host)
       for (int j = 0; j < it.n_kv && !aborted; ++j, ++g) {
         const int s = (int)(g & 1);
-        if (j * 4 >= win + 32) {
-          win = j * 4;
+        if (j * kSubPerTile >= win + 32) {
+          win = j * kSubPerTile;
           const int sb = win + lane;  // sub-block index within the sequence
           const int64_t col = sb / spb;
           int32_t blk = -1;
@@ -460,14 +607,16 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
             set_device_error(p.err, B2P_DEV_BLOCK_RANGE);
             blk = -1;
           }
-          my_slot = blk < 0 ? num_slots : (int64_t)blk * p.block_size + (int64_t)(sb % spb) * kSub;
+          my_slot = (int32_t)(blk < 0 ? num_slots : (int64_t)blk * p.block_size + (int64_t)(sb % spb) * kSub);
         }
-        int64_t slots[4];
+        int32_t slots[kSubPerTile];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) slots[u] = __shfl_sync(0xffffffffu, my_slot, j * 4 - win + u);
+        for (int u = 0; u < kSubPerTile; ++u)
+          slots[u] = __shfl_sync(0xffffffffu, my_slot, j * kSubPerTile - win + u);
         if (lane == 0) {
-          // K(g) first, then V(g - 1): K stages free up as soon as their QK^T MMAs finish, so
-          // the next K load is in flight while the softmax of the current tile runs.
+          // K(g), then V(g). V(g) waits for PV_B(g - 2), which the MMA warp issues before
+          // QK_B(g - 1), the MMA that K(g + 1) waits for: issuing V right behind K never
+          // holds up the next K.
           if (g >= 2 && !mbar_wait_bounded(&k_empty[s], (uint32_t)(((g >> 1) - 1) & 1), p.err)) {
             aborted = true;
           } else if (*abort_flag) {
@@ -476,26 +625,18 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
             uint8_t* kdst = smem + kOffK + s * kKVBytes;
             mbar_arrive_expect_tx(&k_full[s], kKVBytes);
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
+            for (int u = 0; u < kSubPerTile; ++u)
 #pragma unroll
               for (int c = 0; c < 2; ++c)
                 tma_load_5d(kdst + c * (kN * 128) + u * (kSub * 128), &kmap, &k_full[s], 0, c,
-                            kvh, (int)slots[u], p.layer);
+                            kvh, slots[u], p.layer);
             misc[2] = (int)(g + 1);  // K tiles issued
-            if (j > 0 && !issue_v(g - 1, v_slots, kvh)) aborted = true;
+            if (!issue_v(g, slots, kvh)) aborted = true;
           }
           if (aborted) *abort_flag = 1;
-#pragma unroll
-          for (int u = 0; u < 4; ++u) v_slots[u] = slots[u];
         }
         aborted = __shfl_sync(0xffffffffu, aborted ? 1 : 0, 0) != 0;
       }
-      // the item's last V tile
-      if (lane == 0 && !aborted && !issue_v(g - 1, v_slots, kvh)) {
-        *abort_flag = 1;
-        aborted = true;
-      }
-      aborted = __shfl_sync(0xffffffffu, aborted ? 1 : 0, 0) != 0;
       if (aborted) break;
     }
     if (aborted && lane == 0) {  // the consumers learn it from the flag or their waits
@@ -505,67 +646,91 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
     // ---------------------------------------------------------------- MMA issuer
     const uint32_t id_qk = idesc_f16(ab, kM, kN, 0, 0);
     const uint32_t id_pv = idesc_f16(ab, kM, kD, 0, 1);
-    const uint32_t q_addr = smem_u32(smem + kOffQ);
     int64_t g = 0;
     int nq = 0;
+    int n0 = 0, n1 = 0;  // PV MMAs issued for head A / head B (S, P and O barrier phases)
     bool ok = true;
     for (int i = 0; ok; ++i) {
       ItemInfo it;
       if (!take_item(i, it)) break;
       if (it.n_kv == 0) continue;
+      const int nh = it.qh_b >= 0 ? 2 : 1;
       if (lane == 0) {
-        auto issue_qk = [&](int64_t gg) {
-          const int s = (int)(gg & 1);
-          const uint32_t k_addr = smem_u32(smem + kOffK + s * kKVBytes);
-          const uint32_t d = tbase + (s ? kColS1 : kColS0);
+        auto issue_qk = [&](int h, int64_t gg) {
+          const uint32_t q_addr = smem_u32(smem + kOffQ + h * kQBytes);
+          const uint32_t k_addr = smem_u32(smem + kOffK + (int)(gg & 1) * kKVBytes);
+          const uint32_t d = tbase + col_s(h);
 #pragma unroll
           for (int kk = 0; kk < kD / 16; ++kk) {
             const uint64_t da = smem_desc_sw128(q_addr + (kk >> 2) * (kM * 128) + (kk & 3) * 32, 16, 1024);
             const uint64_t db = smem_desc_sw128(k_addr + (kk >> 2) * (kN * 128) + (kk & 3) * 32, 16, 1024);
             mma_ss(d, da, db, id_qk, kk > 0 ? 1u : 0u);
           }
-          mma_commit(&s_full[s]);
-          mma_commit(&k_empty[s]);  // K stage s is free once these MMAs have read it
+          mma_commit(&s_full[h]);
         };
-        // S buffer g & 1 held P of tile g - 2: PV(g - 2) must be done reading it.
-        auto s_free = [&](int64_t gg) -> bool {
-          return gg < 2 || mbar_wait_bounded(&o_done[(gg - 2) & 1], (uint32_t)(((gg - 2) >> 1) & 1), p.err);
+        auto issue_pv = [&](int h, int64_t gg, bool first) {
+          const uint32_t v_addr = smem_u32(smem + kOffV + (int)(gg & 1) * kKVBytes);
+          const uint32_t p_tmem = tbase + col_s(h) + kColP;
+#pragma unroll
+          for (int kk = 0; kk < kN / 16; ++kk) {
+            const uint64_t db = smem_desc_sw128(v_addr + kk * (16 * 128), kN * 128, 1024);
+            mma_ts(tbase + col_o(h), p_tmem + kk * 8, db, id_pv, (!first || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&o_done[h]);
+        };
+        // S of head h is free once the PV MMA of its previous tile has read P.
+        auto s_free = [&](int h) -> bool {
+          const int n = h ? n1 : n0;
+          return n == 0 || mbar_wait_bounded(&o_done[h], (uint32_t)((n - 1) & 1), p.err);
         };
         ok = mbar_wait_bounded(q_full, (uint32_t)(nq & 1), p.err);
-        if (ok) ok = s_free(g) && mbar_wait_bounded(&k_full[g & 1], (uint32_t)((g >> 1) & 1), p.err);
+        if (ok) ok = mbar_wait_bounded(&k_full[g & 1], (uint32_t)((g >> 1) & 1), p.err);
+        for (int h = 0; h < nh && ok; ++h) {
+          ok = s_free(h);
+          if (ok) {
+            tc_fence_after();
+            issue_qk(h, g);
+          }
+        }
         if (ok) {
-          tc_fence_after();
-          issue_qk(g);
+          mma_commit(&k_empty[g & 1]);
           if (it.n_kv == 1) mma_commit(q_empty);  // the item's last read of Q
         }
         for (int j = 0; j < it.n_kv && ok && !*abort_flag; ++j, ++g) {
           const int s = (int)(g & 1);
-          if (j + 1 < it.n_kv) {
-            ok = s_free(g + 1) &&
-                 mbar_wait_bounded(&k_full[(g + 1) & 1], (uint32_t)(((g + 1) >> 1) & 1), p.err);
+          const bool more = j + 1 < it.n_kv;
+          ok = mbar_wait_bounded(&v_full[s], (uint32_t)((g >> 1) & 1), p.err);
+          // PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1): each head's next S is computed while
+          // the other head's softmax runs.
+          for (int h = 0; h < nh && ok; ++h) {
+            const int n = h ? n1 : n0;
+            ok = mbar_wait_bounded(&p_full[h], (uint32_t)(n & 1), p.err);
             if (!ok) break;
             tc_fence_after();
-            issue_qk(g + 1);
+            issue_pv(h, g, j == 0);
+            if (h) ++n1; else ++n0;
+            if (more) {
+              if (h == 0)
+                ok = mbar_wait_bounded(&k_full[(g + 1) & 1], (uint32_t)(((g + 1) >> 1) & 1), p.err);
+              ok = ok && s_free(h);
+              if (!ok) break;
+              tc_fence_after();
+              issue_qk(h, g + 1);
+            }
+          }
+          if (!ok) break;
+          if (more) {
+            mma_commit(&k_empty[(g + 1) & 1]);
             if (j + 2 == it.n_kv) mma_commit(q_empty);
           }
-          ok = mbar_wait_bounded(&p_full[s], (uint32_t)((g >> 1) & 1), p.err);
-          if (ok) ok = mbar_wait_bounded(&v_full[s], (uint32_t)((g >> 1) & 1), p.err);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t v_addr = smem_u32(smem + kOffV + s * kKVBytes);
-          const uint32_t p_tmem = tbase + (s ? kColS1 : kColS0);
-#pragma unroll
-          for (int kk = 0; kk < kN / 16; ++kk) {
-            const uint64_t db = smem_desc_sw128(v_addr + kk * (16 * 128), kN * 128, 1024);
-            mma_ts(tbase + kColO, p_tmem + kk * 8, db, id_pv, (j > 0 || kk > 0) ? 1u : 0u);
-          }
           mma_commit(&v_empty[s]);
-          mma_commit(&o_done[s]);
         }
         if (!ok) *abort_flag = 1;
       }
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       g = __shfl_sync(0xffffffffu, g, 0);
+      n0 = __shfl_sync(0xffffffffu, n0, 0);
+      n1 = __shfl_sync(0xffffffffu, n1, 0);
       ++nq;
     }
     if (lane == 0) {
@@ -575,79 +740,147 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
     }
   } else {
     // ---------------------------------------------------------------- softmax + epilogue
+    const int h = (warp - 2) >> 2;      // 0: head A, 1: head B
     const int quarter = warp & 3;        // TMEM lanes 32*quarter .. +31
     const int row = quarter * 32 + lane;  // query row within the tile
     const uint32_t lane_base = tbase + ((uint32_t)(quarter * 32) << 16);
-    int64_t g = 0;
+    const uint32_t s_col = lane_base + col_s(h);
+    const uint32_t o_col = lane_base + col_o(h);
+    int64_t g = 0;  // K/V tiles of the items seen so far (V stage of the tail fix-up)
+    int n = 0;      // tiles of this head so far (S, P and O barrier phases)
     bool ok = true;
     for (int i = 0; ok; ++i) {
       ItemInfo it;
       if (!take_item(i, it)) break;
       if (it.n_kv == 0) continue;
+      if (h == 1 && it.qh_b < 0) {  // an odd group's last head: head A alone
+        g += it.n_kv;
+        continue;
+      }
+      const int qh = h ? it.qh_b : it.qh_a;
       const bool valid_row = row < it.rows_valid;
       const int pos = it.pos0 + row;
       float m = -INFINITY, l = 0.f;
-      for (int j = 0; j < it.n_kv; ++j, ++g) {
-        const int s = (int)(g & 1);
-        if (ok && !mbar_wait_bounded(&s_full[s], (uint32_t)((g >> 1) & 1), p.err)) ok = false;
+      for (int j = 0; j < it.n_kv; ++j, ++g, ++n) {
+        if (ok && !mbar_wait_bounded(&s_full[h], (uint32_t)(n & 1), p.err)) ok = false;
         ok = __all_sync(0xffffffffu, ok);
         if (!ok || *abort_flag) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t s_col = lane_base + (s ? kColS1 : kColS0);
-        uint32_t r0[32], r1[32];
-        tmem_ld32(s_col, r0);
-        tmem_ld32(s_col + 32, r1);
-        tmem_wait_ld();
         const int key0 = j * kN;
-        // key c of this tile is visible iff key0 + c <= pos (then also < ctx). Tiles that
-        // every row of the warp sees whole (all but the diagonal ones) skip the masks.
-        const int nvis = valid_row ? min(kN, pos - key0 + 1) : 0;
-        const bool whole = __all_sync(0xffffffffu, nvis == kN);
-        float mx = whole ? row_max64<false>(r0, r1, nvis) : row_max64<true>(r0, r1, nvis);
-        mx = mx * p.scale_log2;  // scale_log2 > 0 keeps the arg-max
-        bool rescale = false;
-        float alpha = 1.f;
-        if (mx > -INFINITY) {
-          if (m == -INFINITY) {
-            m = mx;
-          } else if (mx > m + kRescaleThreshold) {
-            alpha = fast_exp2(m - mx);
-            m = mx;
-            rescale = true;
-          }
-        }
-        // Rows that move their reference max fix O once PV of the previous tile has landed.
-        if (__any_sync(0xffffffffu, rescale)) {
-          if (!mbar_wait_bounded(&o_done[(g - 1) & 1], (uint32_t)(((g - 1) >> 1) & 1), p.err)) ok = false;
+        // key c of this tile is visible iff key0 + c <= pos (then also < ctx). Halves that
+        // every row of the warp sees whole (all but the diagonal tiles) skip the masks.
+        const int nv0 = valid_row ? pos - key0 + 1 : 0;  // visible keys from column 0
+        const int nv1 = nv0 - 64;                        // ... from column 64
+        const bool whole0 = __all_sync(0xffffffffu, nv0 >= 64);
+        const bool whole1 = __all_sync(0xffffffffu, nv1 >= 64);
+        uint32_t r0[32], r1[32], pk[32];  // S of a 64-key half, its P
+        float rs1, rs0;
+        // O *= alpha (per row) once PV of the previous tile has landed; l follows.
+        auto rescale_o = [&](float alpha) -> bool {
+          if (!mbar_wait_bounded(&o_done[h], (uint32_t)((n - 1) & 1), p.err)) ok = false;
           ok = __all_sync(0xffffffffu, ok);
-          if (!ok) break;
+          if (!ok) return false;
           tc_fence_after();
-          for (int c0 = 0; c0 < kD; c0 += 32) {
-            uint32_t o[32];
-            tmem_ld32(lane_base + kColO + c0, o);
+          for (int c0 = 0; c0 < kD; c0 += 16) {  // 16 columns at a time: S/P stay live
+            uint32_t o[16];
+            tmem_ld16(o_col + c0, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-            tmem_st32(lane_base + kColO + c0, o);
+            for (int c = 0; c < 16; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+            tmem_st16(o_col + c0, o);
           }
           tmem_wait_st();
           l *= alpha;
+          return true;
+        };
+        auto exp_half = [&](bool whole, int nv) -> float {
+          return whole ? row_exp64<T, false>(r0, r1, nv, p.scale_log2, m, pk)
+                       : row_exp64<T, true>(r0, r1, nv, p.scale_log2, m, pk);
+        };
+        // Largest S * scale_log2 - m over the visible keys of the half in r0/r1.
+        auto xmax_half = [&](bool whole, int nv) -> float {
+          const float mx = whole ? row_max64<false>(r0, r1, nv) : row_max64<true>(r0, r1, nv);
+          return mx * p.scale_log2 - m;
+        };
+        if (j == 0) {
+          // First tile of the item: the reference max comes from the tile (two passes; keys
+          // 64..127 are left in registers, their columns then take their P).
+          tmem_ld32(s_col, r0);
+          tmem_ld32(s_col + 32, r1);
+          tmem_wait_ld();
+          float mx = whole0 ? row_max64<false>(r0, r1, nv0) : row_max64<true>(r0, r1, nv0);
+          tmem_ld32(s_col + 64, r0);
+          tmem_ld32(s_col + 96, r1);
+          tmem_wait_ld();
+          mx = fmaxf(mx, whole1 ? row_max64<false>(r0, r1, nv1) : row_max64<true>(r0, r1, nv1));
+          m = mx * p.scale_log2;  // scale_log2 > 0 keeps the arg-max; -inf for empty rows
+          rs1 = exp_half(whole1, nv1);
+          tmem_st32(s_col + kColP + 32, pk);
+          tmem_ld32(s_col, r0);
+          tmem_ld32(s_col + 32, r1);
+          tmem_wait_ld();
+          rs0 = exp_half(whole0, nv0);
+        } else {
+          // Later tiles: one pass per half with the running reference m. exp2(x - m) is
+          // exact for any reference as long as x = S * scale - m stays small. A half's sum
+          // is at most 64 * 2^8 when every x <= 8 and above 2^8 when any x > 8 (or on
+          // overflow), so rows whose sum passes 2^8 recompute the true max and, where it
+          // passes the threshold, move m (O, l and P already stored are rescaled).
+          constexpr float kSumCheck = 256.f;
+          tmem_ld32(s_col + 64, r0);
+          tmem_ld32(s_col + 96, r1);
+          tmem_wait_ld();
+          rs1 = exp_half(whole1, nv1);
+          if (__any_sync(0xffffffffu, !(rs1 <= kSumCheck))) {
+            const float xm = xmax_half(whole1, nv1);
+            const bool mv = xm > kRescaleThreshold;
+            if (__any_sync(0xffffffffu, mv)) {
+              const float alpha = mv ? fast_exp2(-xm) : 1.f;
+              if (mv) m += xm;
+              if (!rescale_o(alpha)) break;
+              rs1 = exp_half(whole1, nv1);
+            }
+          }
+          tmem_st32(s_col + kColP + 32, pk);
+          tmem_ld32(s_col, r0);
+          tmem_ld32(s_col + 32, r1);
+          tmem_wait_ld();
+          rs0 = exp_half(whole0, nv0);
+          if (__any_sync(0xffffffffu, !(rs0 <= kSumCheck))) {
+            const float xm = xmax_half(whole0, nv0);
+            const bool mv = xm > kRescaleThreshold;
+            if (__any_sync(0xffffffffu, mv)) {
+              const float alpha = mv ? fast_exp2(-xm) : 1.f;
+              if (mv) m += xm;
+              if (!rescale_o(alpha)) break;
+              rs1 *= alpha;
+              tmem_wait_st();
+              for (int c0 = 0; c0 < 32; c0 += 16) {
+                uint32_t pv[16];
+                tmem_ld16(s_col + kColP + 32 + c0, pv);
+                tmem_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 16; ++c) pv[c] = scale_pair<T>(pv[c], alpha);
+                tmem_st16(s_col + kColP + 32 + c0, pv);
+              }
+              rs0 = exp_half(whole0, nv0);
+            }
+          }
         }
-        uint32_t pk[32];
-        const float rs = whole ? row_exp64<T, false>(r0, r1, nvis, p.scale_log2, m, pk)
-                               : row_exp64<T, true>(r0, r1, nvis, p.scale_log2, m, pk);
-        l += rs;
-        tmem_st32(s_col, pk);
+        tmem_st32(s_col + kColP, pk);
+        l += rs1 + rs0;
         tmem_wait_st();
         // Keys past the context (the last KV tile's tail) may hold NaN/Inf in the pool;
-        // P is 0 there but 0 * NaN is not: zero those V rows before the PV MMA reads them.
+        // P is 0 there but 0 * NaN is not: zero those V rows before the PV MMAs read them.
+        // Head A's warps do it; head B's PV is issued after head A's.
         const int tail0 = it.ctx - key0;  // first row of this tile past the context
-        if (j == it.n_kv - 1 && tail0 < kN) {
-          if (!mbar_wait_bounded(&v_full[s], (uint32_t)((g >> 1) & 1), p.err)) ok = false;
-          uint8_t* vt = smem + kOffV + s * kKVBytes;
+        if (h == 0 && j == it.n_kv - 1 && tail0 < kN) {
+          const int64_t gv = g;
+          if (!mbar_wait_bounded(&v_full[gv & 1], (uint32_t)((gv >> 1) & 1), p.err)) ok = false;
+          uint8_t* vt = smem + kOffV + (int)(gv & 1) * kKVBytes;
           const int zrows = kN - max(tail0, 0);
           for (int e = threadIdx.x - 64; e < 2 * zrows * 8; e += 128) {
             const int c = e / (zrows * 8);         // d chunk
@@ -659,33 +892,46 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
           fence_proxy_async_smem();
         }
         tc_fence_before();
-        mbar_arrive(&p_full[s]);
+        mbar_arrive(&p_full[h]);
       }
-      // ---- epilogue: O / l -> out (the next item's first PV waits for this warp's arrival
-      // on its first P, which comes after these reads)
+      // ---- epilogue: O / l -> out (the next item's first PV of this head waits for this
+      // warp's arrival on its first P, which comes after these reads)
       if (ok) {
-        const int64_t gl = g - 1;
-        if (!mbar_wait_bounded(&o_done[gl & 1], (uint32_t)((gl >> 1) & 1), p.err)) ok = false;
+        if (!mbar_wait_bounded(&o_done[h], (uint32_t)((n - 1) & 1), p.err)) ok = false;
         ok = __all_sync(0xffffffffu, ok);
       }
       if (ok) {
         tc_fence_after();
         const float inv = l > 0.f ? 1.f / l : 0.f;
-        T* orow = reinterpret_cast<T*>(p.out) + (int64_t)(it.q0 + it.qt * kM + row) * p.o_tok +
-                  (int64_t)it.qh * p.o_head;
+        // 32 columns at a time: each thread puts its row's 64 bytes in the warp's staging
+        // buffer (16-byte pieces XOR-swizzled by row), then the warp writes 8 rows x 64 B
+        // per store instruction instead of 32 scattered rows.
+        uint8_t* stage = smem + kOffStage + (warp - 2) * kStageBytes;
+        const int64_t row0 = (int64_t)it.q0 + it.qt * kM + quarter * 32;  // this warp's rows
+        const int nrows = min(32, it.rows_valid - quarter * 32);
+        T* obase = reinterpret_cast<T*>(p.out) + (int64_t)qh * p.o_head;
         for (int c0 = 0; c0 < kD; c0 += 32) {
           uint32_t o[32];
-          tmem_ld32(lane_base + kColO + c0, o);
+          tmem_ld32(o_col + c0, o);
           tmem_wait_ld();
-          if (valid_row) {
-            uint32_t pk[16];
+          uint32_t pk[16];
 #pragma unroll
-            for (int c = 0; c < 16; ++c)
-              pk[c] = pack2<T>(__uint_as_float(o[2 * c]) * inv, __uint_as_float(o[2 * c + 1]) * inv);
+          for (int c = 0; c < 16; ++c)
+            pk[c] = pack2<T>(__uint_as_float(o[2 * c]) * inv, __uint_as_float(o[2 * c + 1]) * inv);
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-              reinterpret_cast<uint4*>(orow + c0)[c] = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(stage + lane * 64 + ((c ^ ((lane >> 1) & 3)) * 16)) =
+                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int pass = 0; pass < 4; ++pass) {
+            const int r = pass * 8 + (lane >> 2);
+            const int c = lane & 3;
+            if (r < nrows)
+              *reinterpret_cast<uint4*>(obase + (row0 + r) * p.o_tok + c0 + c * 8) =
+                  *reinterpret_cast<const uint4*>(stage + r * 64 + ((c ^ ((r >> 1) & 3)) * 16));
           }
+          __syncwarp();
         }
         tc_fence_before();
       }
@@ -696,8 +942,8 @@ __global__ void __launch_bounds__(kThreads, 2) paged_prefill_tc(const __grid_con
   // ---- teardown: every TMA and MMA of this CTA has finished before TMEM is freed
   __syncthreads();
   if (warp == 0 && lane == 0) {
-    // Loads this CTA issued land before it leaves: the last Q tile, and the last two K/V
-    // tiles (at most two are ever in flight).
+    // Loads this CTA issued land before it leaves: the last Q tiles, and the last two K and
+    // V tiles (at most two of each are ever in flight).
     const int nq_issued = misc[1];
     if (nq_issued > 0) mbar_wait_bounded(q_full, (uint32_t)((nq_issued - 1) & 1), nullptr);
     const int k_issued = misc[2];
@@ -809,12 +1055,8 @@ int b2p_prefill_tc(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
   e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
                            cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) return b2p_host::record_error(e);
-  // Persistent: every resident CTA walks the work items (tile-items x query heads). The
-  // residency comes from the SM's own limits (shared memory with the per-CTA reservation,
-  // the register file, tensor memory: two CTAs' 256 columns fill it), computed once per
-  // device. cudaOccupancyMaxActiveBlocksPerMultiprocessor answers 1 for this kernel on
-  // B200 although two CTAs run side by side (measured: 296 CTAs started within 1 us on
-  // 148 SMs, at TMEM columns 0 and 256), and a grid of one CTA per SM ran 1.6x slower.
+  // Persistent: one CTA per SM walks the work items (its 512 TMEM columns and ~194 KB of
+  // shared memory fill the SM). The SM's limits are checked once per device.
   static int resident[64] = {0};
   int dev = 0;
   e = cudaGetDevice(&dev);
@@ -833,15 +1075,12 @@ int b2p_prefill_tc(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
       return b2p_host::record_error(e);
     // registers are handed out per warp in 256-register units
     const int warp_regs = (fa.numRegs * 32 + 255) / 256 * 256;
-    const int by_regs = regs_sm / (warp_regs * (kThreads / 32));
-    const int by_smem = smem_sm / (smem + (int)fa.sharedSizeBytes + reserved);
-    int n = by_regs < by_smem ? by_regs : by_smem;
-    if (n > 2) n = 2;
-    resident[dev] = n;
+    const bool fits = regs_sm >= warp_regs * (kThreads / 32) &&
+                      smem_sm >= smem + (int)fa.sharedSizeBytes + reserved;
+    resident[dev] = fits ? 1 : -1;
   }
-  const int per_sm = resident[dev];
-  if (per_sm <= 0) return B2P_EUNSUPPORTED;
-  dim3 grid((unsigned)(b2p_host::sm_count() * per_sm));
+  if (resident[dev] < 0) return B2P_EUNSUPPORTED;
+  dim3 grid((unsigned)b2p_host::sm_count());
   void* args[] = {&qmap, &kmap, &vmap, &p};
   e = cudaLaunchKernel(fn, grid, dim3(kThreads), args, (size_t)smem,
                        static_cast<cudaStream_t>(stream));

@@ -354,7 +354,9 @@ def test_decode_long_context_churned_tables_7b_shape(ops):
 
 # ------------------------------------------------------------------ K3 prefill
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-@pytest.mark.parametrize("shape", [(12, 2, 128, 16), (14, 2, 64, 16), (28, 4, 128, 32)])
+@pytest.mark.parametrize("shape", [(12, 2, 128, 16), (14, 2, 64, 16), (28, 4, 128, 32),
+                                   (6, 2, 128, 16),   # odd GQA group: a lone head per group
+                                   (4, 4, 128, 16)])  # no GQA: every query head alone
 def test_prefill_matches_oracle(ops, dtype, shape):
     hq, hkv, d, bs = shape
     dev = torch.device("cuda")
@@ -417,7 +419,7 @@ def test_metadata_bit_exact(ops):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_prefill_tensor_core_long_prompts_and_chunks(ops, dtype):
-    """Prompts up to 2,100 tokens (several 128-row tiles, many 64-key tiles), fragmented
+    """Prompts up to 2,100 tokens (several 128-row tiles, many 128-key tiles), fragmented
     blocks, whole-history and chunked runs, NaN in the pool slots past every context."""
     hq, hkv, d, bs = 12, 2, 128, 16
     dev = torch.device("cuda")
@@ -442,6 +444,51 @@ def test_prefill_tensor_core_long_prompts_and_chunks(ops, dtype):
     assert int(err.item()) == 0
     assert torch.isfinite(out.float()).all()
     close(out, ref.prefill_attention(q, kc, vc, 0, tables, cu, ctx, bs, d ** -0.5), dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_prefill_running_max_jumps(ops, dtype):
+    """Scores that grow along the keys, so rows keep finding a larger max in later KV tiles
+    (the kernel moves its reference max and rescales O, l and stored P). In the first
+    prompt the larger half of every 128-key tile is keys 64..127, in the second keys
+    0..63; the third grows smoothly; the fourth is a chunked prefill.
+
+    Such peaked rows put most of the weight on a few V rows, so the bf16 rounding of P and
+    V shows up in the max error: 2.4e-2 against the fp32 oracle for this input, the same
+    for a kernel that takes each tile's exact max before the exponentials. The bf16 max
+    bound here is 3e-2 (mean and f16 bounds as elsewhere)."""
+    hq, hkv, d, bs = 12, 2, 128, 16
+    dev = torch.device("cuda")
+    ctx = [900, 777, 1300, 1000]
+    qlen = [900, 777, 1300, 300]
+    cu = np.concatenate([[0], np.cumsum(qlen)]).tolist()
+    nb = sum((c + bs - 1) // bs for c in ctx) + 3
+    kc, vc = make_pool(91, 1, nb, bs, hkv, d, torch.float32)
+    tables, bt = make_tables(92, ctx, bs, nb)
+    for i, (t, c) in enumerate(zip(tables, ctx)):
+        pos = np.arange(c)
+        tile, half = pos // 128, (pos % 128) // 64
+        if i == 0:
+            mult = 1.0 + 2.5 * tile + 1.5 * half
+        elif i == 1:
+            mult = 1.0 + 2.5 * tile + 1.5 * (1 - half)
+        else:
+            mult = 1.0 + pos / 40.0
+        slots = np.array(t)[pos // bs] * bs + pos % bs
+        kc[0, torch.from_numpy(slots)] *= torch.from_numpy(mult).float()[:, None, None]
+    kc, vc = kc.to(dtype), vc.to(dtype)
+    q = torch.randn(cu[-1], hq, d, generator=torch.Generator().manual_seed(93)).to(dtype)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = ops.paged_prefill(q.to(dev), kc.to(dev), vc.to(dev), 0, bt.to(dev),
+                            torch.tensor(cu, dtype=torch.int32, device=dev),
+                            torch.tensor(ctx, dtype=torch.int32, device=dev), max(qlen), bs,
+                            d ** -0.5, err_flag=err)
+    assert int(err.item()) == 0
+    assert torch.isfinite(out.float()).all()
+    expect = ref.prefill_attention(q, kc, vc, 0, tables, cu, ctx, bs, d ** -0.5)
+    diff = (out.float().cpu() - expect).abs()
+    assert diff.max().item() < (3e-2 if dtype == torch.bfloat16 else BF16_MAX), diff.max().item()
+    assert diff.mean().item() < BF16_MEAN, diff.mean().item()
 
 
 def test_prefill_trailing_slice_of_packed_batch(ops):
