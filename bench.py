@@ -55,9 +55,12 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of K2 on this
-# workload, from one ncu capture of a K2 launch over the same sequences and block tables
-# (profiles/paged_decode_tc_decode256.md): 616.06 MB read + 6.83 MB written.
+# workload, from one ncu capture of a K2 launch over the same sequences and block tables:
+# 616.06 MB read + 6.83 MB written.
 K2_TRAFFIC_BYTES: float | None = 622.887936e6
+# The same for K3 on the 32-prompt prefill workload, from one ncu capture of a K3 launch:
+# 240.69 MB read + 121.67 MB written.
+K3_TRAFFIC_BYTES: float | None = 362.35776e6
 
 NUM_SEQS = 256
 CTX_LO, CTX_HI = 512, 4096
@@ -605,7 +608,8 @@ def run_prefill(args) -> None:
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                          "peak_source": "measured bf16_tflops (burst)" if peaks else "fallback",
-                         "traffic": None, "causal_flops": flops, "kernel": "paged_prefill_tc",
+                         "traffic": K3_TRAFFIC_BYTES, "traffic_unit": "bytes per launch",
+                         "causal_flops": flops, "kernel": "paged_prefill_tc",
                          "kernel_us": round(k3_ms * 1e3, 2)},
             "kv_write_us": round((ms - k3_ms) * 1e3, 2),
             "e2e": {"value": round(tokens * world / (e2e_ms / 1e3), 1), "unit": "tok/s",
