@@ -15,7 +15,8 @@ is needed between launches.
            ranks).
 ``e2e``    the same metric through the public ops API with pinned HOST buffers: each step
            copies q, the new K/V rows, block tables and context lengths host->device and
-           the attention output device->host inside the timed region.
+           the attention output device->host inside the timed region (on two side
+           streams, layer by layer, so the copies overlap the other layers' attention).
 ``roofline`` HBM bytes the decode kernel must move per launch (1,024 B x sum(ctx) of K+V,
            plus Q/O, the new K/V rows read and stored, and block tables) / its average
            launch time (CUDA events around every launch of the timed region), against the
@@ -61,6 +62,8 @@ K2_TRAFFIC_BYTES: float | None = 622.887936e6
 # The same for K3 on the 32-prompt prefill workload, from one ncu capture of a K3 launch:
 # 240.69 MB read + 121.67 MB written.
 K3_TRAFFIC_BYTES: float | None = 362.35776e6
+# Prompt groups of the prefill e2e leg (copies of one group overlap another's compute).
+E2E_GROUPS = 4
 
 NUM_SEQS = 256
 CTX_LO, CTX_HI = 512, 4096
@@ -281,17 +284,40 @@ def run_ours(args) -> None:
     h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_tables, h_ctx))
     d2h = h_out.numel() * h_out.element_size()
 
+    # Device landing buffers, and two side streams: layer l + 1's inputs cross PCIe while
+    # layer l computes, and each layer's output goes back as soon as it is ready. A step
+    # starts its copies when the previous step has finished and ends with its last output
+    # on the host, so every byte of the step is inside the timed region.
+    dt, dc = torch.empty_like(tables), torch.empty(h_ctx.shape, dtype=h_ctx.dtype, device=dev)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(new_k), torch.empty_like(new_v)
+    copy_in, copy_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
     def e2e_step():
-        dt = h_tables.to(dev, non_blocking=True)
-        dc = h_ctx.to(dev, non_blocking=True)
-        dq = h_q.to(dev, non_blocking=True)
-        dk = h_k.to(dev, non_blocking=True)
-        dv = h_v.to(dev, non_blocking=True)
+        start = torch.cuda.Event()
+        start.record(stream)
+        copy_in.wait_event(start)
+        landed = []
+        with torch.cuda.stream(copy_in):
+            dt.copy_(h_tables, non_blocking=True)
+            dc.copy_(h_ctx, non_blocking=True)
+            for layer in range(L):
+                dq[layer].copy_(h_q[layer], non_blocking=True)
+                dk[layer].copy_(h_k[layer], non_blocking=True)
+                dv[layer].copy_(h_v[layer], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(copy_in)
+                landed.append(ev)
         for layer in range(L):
+            stream.wait_event(landed[layer])
             ops.paged_decode_append(dq[layer], dk[layer], dv[layer], kc, vc, layer, dt, dc,
                                     BLOCK_SIZE, scale, out=out[layer], workspace=ws,
                                     err_flag=err)
-        h_out.copy_(out, non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(stream)
+            copy_out.wait_event(done)
+            with torch.cuda.stream(copy_out):
+                h_out[layer].copy_(out[layer], non_blocking=True)
+        stream.wait_stream(copy_out)
 
     for _ in range(args.warmup):
         e2e_step()
@@ -564,9 +590,55 @@ def run_prefill(args) -> None:
     h2d = sum(t.numel() * t.element_size() for t in host)
     d2h = h_out.numel() * h_out.element_size()
 
+    # The step runs as four groups of whole prompts (about equal token counts): a group's
+    # inputs cross PCIe on one side stream while the previous group computes, and its
+    # output goes back on another, so the two copy directions overlap. A step starts its
+    # copies when the previous step has finished and ends with its last output on the host.
+    lens_all = w["lens"].astype(np.int64)
+    cu_all = np.concatenate([[0], np.cumsum(lens_all)])
+    cuts = [0]
+    for g in range(1, E2E_GROUPS):
+        cuts.append(int(np.searchsorted(cu_all, cu_all[-1] * g / E2E_GROUPS)))
+    cuts.append(len(lens_all))
+    cuts = sorted(set(cuts))
+    groups = []
+    for a, b in zip(cuts[:-1], cuts[1:]):
+        t0, t1 = int(cu_all[a]), int(cu_all[b])
+        hq, hk, hv = (host[i][t0:t1] for i in range(3))
+        hs = host[3][t0:t1]
+        ht = host[4][a:b]
+        hcu = torch.from_numpy((cu_all[a:b + 1] - t0).astype(np.int32)).pin_memory()
+        hl = host[6][a:b]
+        dev_bufs = tuple(torch.empty(x.shape, dtype=x.dtype, device=dev)
+                         for x in (hq, hk, hv, hs, ht, hcu, hl))
+        groups.append((t0, t1, (hq, hk, hv, hs, ht, hcu, hl), dev_bufs,
+                       int(lens_all[a:b].max())))
+    copy_in, copy_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
     def e2e_step():
-        step(bufs=tuple(t.to(dev, non_blocking=True) for t in host))
-        h_out.copy_(out, non_blocking=True)
+        start = torch.cuda.Event()
+        start.record(stream)
+        copy_in.wait_event(start)
+        landed = []
+        with torch.cuda.stream(copy_in):
+            for _, _, hb, db, _ in groups:
+                for d, h in zip(db, hb):
+                    d.copy_(h, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(copy_in)
+                landed.append(ev)
+        for (t0, t1, _, db, gmax), ev in zip(groups, landed):
+            stream.wait_event(ev)
+            dq, dk, dv, ds, dtb, dcu, dl = db
+            ops.kv_write(w["kc"], w["vc"], 0, ds, dk, dv, err)
+            ops.paged_prefill(dq, w["kc"], w["vc"], 0, dtb, dcu, dl, gmax, BLOCK_SIZE, scale,
+                              out=out[t0:t1], err_flag=err)
+            done = torch.cuda.Event()
+            done.record(stream)
+            copy_out.wait_event(done)
+            with torch.cuda.stream(copy_out):
+                h_out[t0:t1].copy_(out[t0:t1], non_blocking=True)
+        stream.wait_stream(copy_out)
 
     for _ in range(args.warmup):
         e2e_step()
