@@ -56,9 +56,9 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of K2 on this
-# workload, from one ncu capture of a K2 launch over the same sequences and block tables:
-# 616.06 MB read + 6.83 MB written.
-K2_TRAFFIC_BYTES: float | None = 622.887936e6
+# workload (append mode: the KV write fused in), from one ncu capture of a K2 launch over
+# the same sequences and block tables: 616.60 MB read + 7.20 MB written.
+K2_TRAFFIC_BYTES: float | None = 623.803904e6
 # The same for K3 on the 32-prompt prefill workload, from one ncu capture of a K3 launch:
 # 240.69 MB read + 121.67 MB written.
 K3_TRAFFIC_BYTES: float | None = 362.35776e6
