@@ -11,7 +11,9 @@ class EngineConfiguration:
 
     Same fields, defaults and validation errors as the reference's
     ``EngineConfiguration`` (serving/engine/config.py:6-60), so configurations move
-    between the two engines unchanged.
+    between the two engines unchanged, plus ``enable_chunked_prefill`` (off by default,
+    which keeps the reference's policy): prompts longer than ``max_batched_tokens`` are
+    then admitted and prefilled over several steps in chunks that fit the step's budget.
     """
 
     device: str = "cpu"
@@ -21,6 +23,7 @@ class EngineConfiguration:
     num_blocks: int = 256
     max_batched_tokens: int = 2_048
     seed: int = 0
+    enable_chunked_prefill: bool = False
 
     def __post_init__(self) -> None:
         if not self.device.strip():

@@ -9,6 +9,10 @@ discarded; it will be re-prefilled).
 Differences that do not change results: executions carry their block lists instead of
 a per-token slot tuple (the slots are a pure function of the blocks), and greedy tokens
 are picked with one batched argmax per step instead of one ``.item()`` per sequence.
+
+With ``enable_chunked_prefill`` a prefill execution may cover one chunk of a history
+(``query_length`` tokens ending at position ``length``); only the chunk that completes
+the history yields a token.
 """
 
 from __future__ import annotations
@@ -53,24 +57,38 @@ class Engine:
     def cancel(self, request_id: str) -> bool:
         return self.scheduler.cancel(request_id)
 
-    def _execution(self, sequence: SequenceState, phase: ExecutionPhase) -> ModelExecution:
+    def _execution(self, sequence: SequenceState, phase: ExecutionPhase,
+                   chunk: tuple[int, int] | None = None) -> ModelExecution:
         table = self.scheduler.block_table
+        start, n = chunk if chunk is not None else (None, None)
         return ModelExecution(
             sequence=sequence,
             phase=phase,
             block_ids=table.blocks_for_request(sequence.request.request_id),
             block_size=table.block_size,
+            query_length=n,
+            length=None if chunk is None else start + n,
         )
 
     def step(self) -> tuple[SequenceState, ...]:
         out = self.scheduler.schedule()
         executions = [self._execution(s, ExecutionPhase.DECODE) for s in out.decode_sequences]
-        executions += [self._execution(s, ExecutionPhase.PREFILL) for s in out.prefill_sequences]
+        chunks = out.prefill_chunks or (None,) * len(out.prefill_sequences)
+        executions += [self._execution(s, ExecutionPhase.PREFILL, c)
+                       for s, c in zip(out.prefill_sequences, chunks, strict=True)]
         if not executions:
             return ()
         logits = self.model_runner.forward(executions)
+        # A chunk that leaves part of its history for later steps yields no token.
+        partial = set()
+        if out.prefill_chunks:
+            nd = len(out.decode_sequences)
+            for j, (seq, (_, n)) in enumerate(zip(out.prefill_sequences, out.prefill_chunks,
+                                                  strict=True)):
+                if not self.scheduler.complete_prefill_chunk(seq, n):
+                    partial.add(nd + j)
         greedy_rows = [i for i, ex in enumerate(executions)
-                       if ex.sequence.request.sampling_parameters.greedy]
+                       if i not in partial and ex.sequence.request.sampling_parameters.greedy]
         greedy: dict[int, int] = {}
         if greedy_rows:
             picks = Sampler.greedy_batch(logits[greedy_rows] if len(greedy_rows) != len(executions)
@@ -80,7 +98,7 @@ class Engine:
         eos = self.configuration.eos_token_id
         for i, ex in enumerate(executions):
             seq = ex.sequence
-            if seq.status == SequenceStatus.PREEMPTED:
+            if seq.status == SequenceStatus.PREEMPTED or i in partial:
                 continue
             params = seq.request.sampling_parameters
             token = greedy[i] if i in greedy else self.sampler.sample_token(logits[i], params)

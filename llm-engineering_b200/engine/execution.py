@@ -37,13 +37,19 @@ class ModelExecution:
         block_ids: tuple[int, ...] | None = None,
         block_size: int | None = None,
         query_length: int | None = None,
+        length: int | None = None,
     ) -> None:
         self.sequence = sequence
         self.phase = ExecutionPhase(phase)
         self.block_ids = block_ids
         self.block_size = block_size
-        length = sequence.current_length
-        self.length = length  # history length when the step was scheduled
+        # History covered by this step: the whole sequence, or the positions up to the end
+        # of a prefill chunk.
+        if length is None:
+            length = sequence.current_length
+        if not 1 <= length <= sequence.current_length:
+            raise ValueError("length must be within 1..current_length.")
+        self.length = length
         if slot_ids is None and (block_ids is None or not block_size):
             raise ValueError("ModelExecution needs slot_ids or block_ids with block_size.")
         if slot_ids is not None:
@@ -56,7 +62,8 @@ class ModelExecution:
             raise ValueError("block_ids do not cover the sequence current length.")
         self._slot_ids = slot_ids
         # Query tokens contributed this step. Prefill: the whole history (the reference's
-        # recompute prefill) unless a chunk length is given; decode: the newest token.
+        # recompute prefill) unless a chunk is given (the last ``query_length`` positions of
+        # ``length``); decode: the newest token.
         if query_length is None:
             query_length = length if self.phase is ExecutionPhase.PREFILL else 1
         if not 1 <= query_length <= length:

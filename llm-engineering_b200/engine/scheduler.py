@@ -7,6 +7,12 @@ concurrency limit and the free blocks allow, stopping at the first one that does
 fit. When reserving a block for a generated token runs out of blocks, the most recently
 admitted other running sequence is preempted (blocks freed, put back at the head of the
 waiting queue) and re-prefilled later.
+
+With ``enable_chunked_prefill`` (not in the reference, off by default) a prefill may be
+cut to the step's remaining budget: after the decodes, sequences whose prefill is under
+way continue first (in admission order), then waiting sequences are admitted as before,
+the last one taking whatever budget is left. A sequence decodes once all of its history
+is in the pool; preemption drops the progress and the sequence is re-prefilled later.
 """
 
 from __future__ import annotations
@@ -27,6 +33,9 @@ class SchedulerOutput:
     decode_sequences: tuple[SequenceState, ...]
     prefill_sequences: tuple[SequenceState, ...]
     num_batched_tokens: int
+    # (first position, query tokens) of each prefill, aligned with prefill_sequences; empty
+    # when every prefill covers its whole history (the reference's policy).
+    prefill_chunks: tuple[tuple[int, int], ...] = ()
 
 
 class Scheduler:
@@ -41,6 +50,9 @@ class Scheduler:
         self._finished: list[SequenceState] = []
         self._ids: set[str] = set()
         self._num_preemptions = 0
+        # chunked prefill: positions of each admitted sequence already in the pool, for the
+        # sequences whose prefill is not finished
+        self._prefilled: dict[str, int] = {}
 
     # ------------------------------------------------------------------ views
     @property
@@ -69,13 +81,15 @@ class Scheduler:
             raise ValueError(f"request_id {request.request_id!r} has already been submitted.")
         cfg = self.configuration
         n = len(request.prompt_token_ids)
-        if n > cfg.max_batched_tokens:
-            raise ValueError("Prompt length exceeds max_batched_tokens and cannot be "
-                             "prefilled without chunked prefill.")
         longest = n + request.max_new_tokens - 1  # the last token never needs a KV slot
-        if longest > cfg.max_batched_tokens:
-            raise ValueError("Maximum non-terminal sequence length exceeds max_batched_tokens "
-                             "and cannot be re-prefilled without chunked prefill.")
+        if not cfg.enable_chunked_prefill:
+            if n > cfg.max_batched_tokens:
+                raise ValueError("Prompt length exceeds max_batched_tokens and cannot be "
+                                 "prefilled without chunked prefill.")
+            if longest > cfg.max_batched_tokens:
+                raise ValueError("Maximum non-terminal sequence length exceeds "
+                                 "max_batched_tokens and cannot be re-prefilled without "
+                                 "chunked prefill.")
         if blocks_needed(longest, cfg.block_size) > cfg.num_blocks:
             raise ValueError("Maximum non-terminal sequence length requires more KV-cache "
                              "blocks than the scheduler owns.")
@@ -115,6 +129,8 @@ class Scheduler:
         self._running.append(seq)
 
     def schedule(self) -> SchedulerOutput:
+        if self.configuration.enable_chunked_prefill:
+            return self._schedule_chunked()
         budget = self.configuration.max_batched_tokens
         decode = tuple(self._running)
         budget -= len(decode)
@@ -130,6 +146,51 @@ class Scheduler:
         tokens = len(decode) + sum(s.current_length for s in prefill)
         return SchedulerOutput(decode_sequences=decode, prefill_sequences=tuple(prefill),
                                num_batched_tokens=tokens)
+
+    def _schedule_chunked(self) -> SchedulerOutput:
+        budget = self.configuration.max_batched_tokens
+        decode = tuple(s for s in self._running if s.request.request_id not in self._prefilled)
+        budget -= len(decode)
+        prefill: list[SequenceState] = []
+        chunks: list[tuple[int, int]] = []
+        for seq in self._running:  # prefills under way, in admission order
+            if budget <= 0:
+                break
+            done = self._prefilled.get(seq.request.request_id)
+            if done is None:
+                continue
+            n = min(seq.current_length - done, budget)
+            prefill.append(seq)
+            chunks.append((done, n))
+            budget -= n
+        while self._waiting and budget > 0:
+            head = self._waiting[0]
+            if not self._fits(head):
+                break
+            self._admit(head)
+            self._prefilled[head.request.request_id] = 0
+            n = min(head.current_length, budget)
+            prefill.append(head)
+            chunks.append((0, n))
+            budget -= n
+        tokens = len(decode) + sum(n for _, n in chunks)
+        return SchedulerOutput(decode_sequences=decode, prefill_sequences=tuple(prefill),
+                               num_batched_tokens=tokens, prefill_chunks=tuple(chunks))
+
+    def complete_prefill_chunk(self, sequence: SequenceState, num_tokens: int) -> bool:
+        """Record that ``num_tokens`` more positions of ``sequence`` are in the pool; True
+        when its whole history is (the step's logits then give its next token)."""
+        rid = sequence.request.request_id
+        if rid not in self._prefilled:
+            raise RuntimeError("The sequence has no prefill under way.")
+        done = self._prefilled[rid] + num_tokens
+        if done > sequence.current_length:
+            raise RuntimeError("Prefill chunk runs past the sequence's history.")
+        if done == sequence.current_length:
+            del self._prefilled[rid]
+            return True
+        self._prefilled[rid] = done
+        return False
 
     def reserve_generated_token(self, sequence: SequenceState) -> None:
         if sequence.is_finished:
@@ -163,6 +224,7 @@ class Scheduler:
     # ------------------------------------------------------------------ internals
     def _release(self, seq: SequenceState) -> None:
         self.block_table.free_request(seq.request.request_id)
+        self._prefilled.pop(seq.request.request_id, None)
         self._running = [s for s in self._running if s is not seq]
 
     def _preempt(self, seq: SequenceState) -> None:

@@ -122,3 +122,61 @@ def test_block_pool_fifo_order_and_errors():
         table.slot_for_position("r", 8)
     with pytest.raises(ValueError, match="skips one or more logical blocks"):
         table.append_token("r", 12)
+
+
+# ------------------------------------------------------------------ chunked prefill
+def _run(cfg, requests, runner):
+    engine = eng.Engine(configuration=cfg, model_runner=runner)
+    for r in requests:
+        engine.submit(r)
+    engine.run_until_complete()
+    return engine, {s.request.request_id: list(s.generated_token_ids)
+                    for s in engine.finished_sequences}
+
+
+def test_chunked_prefill_admits_long_prompts_and_splits_them_to_the_budget():
+    cfg = eng.EngineConfiguration(block_size=4, num_blocks=64, max_sequences=4,
+                                  max_batched_tokens=16, enable_chunked_prefill=True)
+    s = eng.Scheduler(cfg)
+    s.submit(eng.Request("long", tuple(range(40)), 3))  # refused without chunked prefill
+    s.submit(eng.Request("short", tuple(range(5)), 2))
+    out = s.schedule()
+    assert [q.request.request_id for q in out.prefill_sequences] == ["long"]
+    assert out.prefill_chunks == ((0, 16),) and out.num_batched_tokens == 16
+    long_seq = out.prefill_sequences[0]
+    assert s.complete_prefill_chunk(long_seq, 16) is False
+    out = s.schedule()  # the prefill under way continues before new admissions
+    assert out.prefill_chunks == ((16, 16),) and not out.decode_sequences
+    assert s.complete_prefill_chunk(long_seq, 16) is False
+    out = s.schedule()  # 8 tokens finish "long", the other 8 start "short"
+    assert [q.request.request_id for q in out.prefill_sequences] == ["long", "short"]
+    assert out.prefill_chunks == ((32, 8), (0, 5)) and out.num_batched_tokens == 13
+    assert s.complete_prefill_chunk(out.prefill_sequences[0], 8) is True
+    with pytest.raises(RuntimeError, match="past the sequence's history"):
+        s.complete_prefill_chunk(out.prefill_sequences[1], 6)
+
+
+def test_chunked_prefill_gives_the_tokens_of_whole_prefill():
+    """The stand-in model's token depends on (request, history length) only, so every
+    request must finish with the same tokens whether its prompt was prefilled whole or in
+    chunks; chunked runs also go through preemption (few blocks)."""
+    rng = np.random.default_rng(5)
+    requests = [eng.Request(request_id=f"r{i}",
+                            prompt_token_ids=tuple(int(x) for x in rng.integers(1, 50, size=n)),
+                            max_new_tokens=m, ignore_eos=True)
+                for i, (n, m) in enumerate([(30, 5), (7, 9), (45, 3), (12, 12), (3, 20)])]
+    whole = eng.EngineConfiguration(block_size=4, num_blocks=200, max_sequences=4,
+                                    max_batched_tokens=64)
+    _, expect = _run(whole, requests, HashRunner(vocab=50))
+    for budget, blocks in ((16, 200), (9, 40), (16, 20)):
+        cfg = eng.EngineConfiguration(block_size=4, num_blocks=blocks, max_sequences=4,
+                                      max_batched_tokens=budget, enable_chunked_prefill=True)
+        runner = HashRunner(vocab=50)
+        engine, got = _run(cfg, requests, runner)
+        assert got == expect, (budget, blocks)
+        for step in runner.calls:
+            assert sum(ex.query_length for ex in step) <= budget
+            for ex in step:
+                assert ex.length - ex.query_length >= 0 and ex.length <= ex.sequence.current_length
+        if blocks == 20:
+            assert engine.scheduler.num_preemptions > 0

@@ -166,6 +166,31 @@ def test_runner_logits_match_for_mixed_step_and_reference_style_slots():
     torch.testing.assert_close(got, want, rtol=1e-5, atol=1e-5)
 
 
+def test_chunked_prefill_runs_give_the_tokens_of_whole_prefill():
+    """Prompts longer than the step budget, prefilled in chunks by this package's engine
+    through the B200 runner (chunked queries attend to the whole history in the pool), give
+    the same greedy tokens as whole-prompt prefill with a budget that fits them."""
+    model = tiny_model(2)
+    bs, nb = 4, 96
+    rng = np.random.default_rng(9)
+    requests = [eng.Request(request_id=f"r{i}",
+                            prompt_token_ids=tuple(int(x) for x in rng.integers(0, 97, size=n)),
+                            max_new_tokens=5, ignore_eos=True)
+                for i, n in enumerate([37, 6, 21, 50])]
+    whole_cfg = eng.EngineConfiguration(block_size=bs, num_blocks=nb, max_sequences=4,
+                                        max_batched_tokens=128)
+    kc, vc = pool(2, nb, bs, 2, 16)
+    whole = B200PagedModelRunner(copy.deepcopy(model), torch.device("cpu"), _Storage(kc, vc, bs),
+                                 kernels=CpuKernels())
+    expect = run_engine(whole, requests, whole_cfg)
+    chunk_cfg = eng.EngineConfiguration(block_size=bs, num_blocks=nb, max_sequences=4,
+                                        max_batched_tokens=12, enable_chunked_prefill=True)
+    kc2, vc2 = pool(2, nb, bs, 2, 16)
+    chunked = B200PagedModelRunner(copy.deepcopy(model), torch.device("cpu"),
+                                   _Storage(kc2, vc2, bs), kernels=CpuKernels())
+    assert run_engine(chunked, requests, chunk_cfg) == expect
+
+
 def test_runner_rejects_empty_batch():
     kc, vc = pool(2, 8, 4, 2, 16)
     ours = B200PagedModelRunner(tiny_model(), torch.device("cpu"), _Storage(kc, vc, 4),

@@ -68,6 +68,30 @@ def test_greedy_tokens_match_reference_engine_config1_fp32():
         assert got[rid] == want, (rid, got[rid], want)
 
 
+def test_chunked_prefill_engine_reproduces_reference_tokens_fp32():
+    """The configuration-1 run again, with chunked prefill and a 48-token step budget (the
+    prompts, 16..128 tokens, mostly span several steps and share them with decodes): the
+    tokens must still be the reference engine's."""
+    golden = json.loads((GOLDEN / "greedy_c1.json").read_text())
+    torch.backends.cuda.matmul.allow_tf32 = False
+    dev = torch.device("cuda")
+    model = c1_model().to(dev)
+    storage = PagedKVStorage(num_layers=24, num_blocks=2048, block_size=16, num_kv_heads=2,
+                             head_dim=64, dtype=torch.float32, device=dev)
+    runner = B200PagedModelRunner(model, dev, storage)
+    cfg = eng.EngineConfiguration(device="cuda", block_size=16, num_blocks=2048, max_sequences=8,
+                                  max_batched_tokens=48, seed=0, enable_chunked_prefill=True)
+    engine = eng.Engine(configuration=cfg, model_runner=runner)
+    for r in golden["requests"]:
+        engine.submit(eng.Request(request_id=r["request_id"], prompt_token_ids=tuple(r["prompt"]),
+                                  max_new_tokens=32, ignore_eos=True))
+    engine.run_until_complete()
+    assert runner.device_error() == 0
+    got = {s.request.request_id: list(s.generated_token_ids) for s in engine.finished_sequences}
+    for rid, want in golden["generated"].items():
+        assert got[rid] == want, (rid, got[rid], want)
+
+
 def small_1p5b_attention_model(seed=0):
     from transformers import Qwen2Config, Qwen2ForCausalLM
 
