@@ -1050,22 +1050,23 @@ int b2p_prefill_tc(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
                        ? reinterpret_cast<const void*>(&paged_prefill_tc<__nv_bfloat16>)
                        : reinterpret_cast<const void*>(&paged_prefill_tc<__half>);
   const int smem = kSmemBytes + 1024;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return b2p_host::record_error(e);
-  e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
-                           cudaSharedmemCarveoutMaxShared);
-  if (e != cudaSuccess) return b2p_host::record_error(e);
-  // Persistent: one CTA per SM walks the work items (its 512 TMEM columns and ~194 KB of
-  // shared memory fill the SM). The SM's limits are checked once per device.
-  static int resident[64] = {0};
+  // Persistent: one CTA per SM walks the work items (its 512 TMEM columns and ~222 KB of
+  // shared memory fill the SM). Once per device and element type: the kernel's
+  // shared-memory attributes, and whether one CTA fits the SM's limits.
+  static int resident[64][2] = {};
   int dev = 0;
-  e = cudaGetDevice(&dev);
+  cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return b2p_host::record_error(e);
   if (dev < 0 || dev >= 64) return B2P_EUNSUPPORTED;
-  if (resident[dev] == 0) {
+  int& fit = resident[dev][dtype == B2P_BF16 ? 0 : 1];
+  if (fit == 0) {
     cudaFuncAttributes fa;
     int smem_sm = 0, reserved = 0, regs_sm = 0;
-    if ((e = cudaFuncGetAttributes(&fa, fn)) != cudaSuccess ||
+    if ((e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) !=
+            cudaSuccess ||
+        (e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                  cudaSharedmemCarveoutMaxShared)) != cudaSuccess ||
+        (e = cudaFuncGetAttributes(&fa, fn)) != cudaSuccess ||
         (e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor,
                                     dev)) != cudaSuccess ||
         (e = cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev)) !=
@@ -1077,9 +1078,9 @@ int b2p_prefill_tc(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
     const int warp_regs = (fa.numRegs * 32 + 255) / 256 * 256;
     const bool fits = regs_sm >= warp_regs * (kThreads / 32) &&
                       smem_sm >= smem + (int)fa.sharedSizeBytes + reserved;
-    resident[dev] = fits ? 1 : -1;
+    fit = fits ? 1 : -1;
   }
-  if (resident[dev] < 0) return B2P_EUNSUPPORTED;
+  if (fit < 0) return B2P_EUNSUPPORTED;
   dim3 grid((unsigned)b2p_host::sm_count());
   void* args[] = {&qmap, &kmap, &vmap, &p};
   e = cudaLaunchKernel(fn, grid, dim3(kThreads), args, (size_t)smem,
