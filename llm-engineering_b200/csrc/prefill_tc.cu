@@ -80,10 +80,10 @@ constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kOffItems = kOffMisc + 64;
 constexpr int kOffStage = (kOffItems + 2 * 48 + 127) / 128 * 128;  // epilogue: 8 warps x 32 rows x 64 B
 constexpr int kStageBytes = 32 * 64;
-constexpr int kSeqCache = 2048;
-constexpr int kRoundCache = 1024;
+constexpr int kSeqCache = 1024;
+constexpr int kSizeCache = 1024;
 constexpr int kOffSched = kOffStage + 8 * kStageBytes;  // scheduler tables
-constexpr int kSmemBytes = kOffSched + (kSeqCache + kRoundCache + 1) * 4;
+constexpr int kSmemBytes = kOffSched + (3 * kSeqCache + kSizeCache + 1) * 4;
 
 // TMEM columns (512 allocated): S of head A at 0, of head B at 128, O_A at 256, O_B at
 // 384. P overwrites the second half of its S (columns +64 .. +127, two keys per column).
@@ -296,23 +296,18 @@ __device__ __forceinline__ uint32_t scale_pair<__half>(uint32_t v, float a) {
   return pack2<__half>(f.x * a, f.y * a);
 }
 
-// Work items. Sequence s has ntiles(s) = ceil(q_len_s / 128) query tiles; tile-items are
-// ordered round by round from the end: round r holds tile ntiles(s) - 1 - r of every
-// sequence with more than r tiles, sequences in index order. A sequence's later tiles see
-// more keys, so the order runs close to longest first (LPT) whatever the prompt mix. Work
-// item k is tile-item k / (HKV * pairs) for head pair k % (HKV * pairs): the query heads of
-// a GQA group go two by two (the last one alone when the group is odd), and the pairs of
-// one tile are neighbours, so the whole group reads the same K/V tiles close together.
+// Work items. Sequence s has ntiles(s) = ceil(q_len_s / 128) query tiles; its tile t
+// needs size(s, t) KV tiles: t + 1 + ceil((ctx_s - q_len_s) / 128) for every full tile and
+// ceil(ctx_s / 128) for the last one. Tile-items are claimed longest first: by size
+// descending, then by sequence, a sequence's full tile before its last tile. Work item k is
+// tile-item k / (HKV * pairs) for head pair k % (HKV * pairs): the query heads of a GQA
+// group go two by two (the last one alone when the group is odd), and the pairs of one
+// tile are neighbours, so the whole group reads the same K/V tiles close together.
 struct ItemInfo {
   int seq;  // -1: no more work for this CTA
   int qt, kvh, qh_a, qh_b;  // qh_b = -1: head A only
   int q0, qlen, ctx, rows_valid, pos0, n_kv, pad;
 };
-
-__device__ __forceinline__ int ntiles_of(const PrefillParams& p, int s) {
-  const int q = __ldg(p.cu_q + s + 1) - __ldg(p.cu_q + s);
-  return q > 0 ? ceil_div(q, kM) : 0;
-}
 
 __device__ __forceinline__ int64_t warp_sum64(int64_t v) {
 #pragma unroll
@@ -320,64 +315,108 @@ __device__ __forceinline__ int64_t warp_sum64(int64_t v) {
   return v;
 }
 
-// Scheduler tables in shared memory, built once per CTA by the producer warp: the tile
-// counts of the first kSeqCache sequences, and the tile-items before each round when the
-// longest sequence has at most kRoundCache tiles. Past either size the scheduler reads
-// cu_seqlens directly (same results, more global round trips per item).
-struct SchedTables {
-  int32_t* nt;      // [kSeqCache]
-  int32_t* before;  // [kRoundCache + 1]
-  bool rounds;      // `before` holds rounds 0..maxnt
+// What the scheduler needs of one sequence: query tiles, the size of its first full tile
+// minus one (c = ceil((ctx - q_len) / 128)), and the size of its last tile.
+struct SeqTiles {
+  int nt, c, last;
 };
 
-__device__ __forceinline__ int nt_of(const PrefillParams& p, const SchedTables& st, int s) {
-  return s < kSeqCache ? st.nt[s] : ntiles_of(p, s);
+__device__ __forceinline__ SeqTiles seq_tiles_global(const PrefillParams& p, int s) {
+  const int q0 = __ldg(p.cu_q + s);
+  const int q = __ldg(p.cu_q + s + 1) - q0;
+  const int ctx = __ldg(p.ctx + s);
+  SeqTiles t;
+  t.nt = q > 0 ? ceil_div(q, kM) : 0;
+  t.c = ctx > q ? ceil_div(ctx - q, kN) : 0;
+  t.last = max(1, ceil_div(max(ctx, 1), kN));
+  return t;
 }
 
-// Tile-items in rounds before r: sum over sequences of min(ntiles, r). One warp.
-__device__ __forceinline__ int64_t items_before_round(const PrefillParams& p, const SchedTables& st, int r,
-                                      int lane) {
-  if (st.rounds) return st.before[r];
+// Tiles of a sequence whose size is larger than v.
+__device__ __forceinline__ int tiles_above(const SeqTiles& t, int v) {
+  if (t.nt == 0) return 0;
+  const int full = max(0, (t.nt - 1 + t.c) - max(v, t.c));  // full sizes 1+c .. nt-1+c
+  return full + (t.last > v ? 1 : 0);
+}
+
+// Scheduler tables in shared memory, built once per CTA by the producer warp: the
+// SeqTiles of the first kSeqCache sequences, and the tile-items larger than each size v
+// when no tile needs more than kSizeCache KV tiles. Past either limit the scheduler reads
+// cu_seqlens and the context lengths directly (same order, more global round trips).
+struct SchedTables {
+  int32_t* seq;     // [kSeqCache][3]: nt, c, last
+  int32_t* above;   // [kSizeCache + 1]: tile-items of size > v
+  bool sizes;       // `above` holds sizes 0..maxv
+};
+
+__device__ __forceinline__ SeqTiles seq_tiles(const PrefillParams& p, const SchedTables& st, int s) {
+  if (s < kSeqCache) return SeqTiles{st.seq[3 * s], st.seq[3 * s + 1], st.seq[3 * s + 2]};
+  return seq_tiles_global(p, s);
+}
+
+// Tile-items larger than v. One warp; all lanes get the result.
+__device__ __forceinline__ int64_t items_above(const PrefillParams& p, const SchedTables& st,
+                                               int v, int lane) {
+  if (st.sizes) return st.above[v];
   int64_t acc = 0;
-  for (int s = lane; s < p.num_seqs; s += 32) acc += min(nt_of(p, st, s), r);
+  for (int s = lane; s < p.num_seqs; s += 32) acc += tiles_above(seq_tiles(p, st, s), v);
   return warp_sum64(acc);
 }
 
-// Fills the tables and returns the total tile-items (all lanes); maxnt gets the longest
-// sequence's tile count. One warp.
-__device__ __forceinline__ int64_t build_sched_tables(const PrefillParams& p, SchedTables& st, int lane,
-                                      int& maxnt) {
+// Fills the tables and returns the total tile-items (all lanes); maxv gets the largest
+// tile size. One warp.
+__device__ __forceinline__ int64_t build_sched_tables(const PrefillParams& p, SchedTables& st,
+                                                      int lane, int& maxv) {
   int64_t total = 0;
-  maxnt = 0;
+  maxv = 0;
   for (int s = lane; s < p.num_seqs; s += 32) {
-    const int nt = ntiles_of(p, s);
-    if (s < kSeqCache) st.nt[s] = nt;
-    total += nt;
-    maxnt = max(maxnt, nt);
+    const SeqTiles t = seq_tiles_global(p, s);
+    if (s < kSeqCache) {
+      st.seq[3 * s] = t.nt;
+      st.seq[3 * s + 1] = t.c;
+      st.seq[3 * s + 2] = t.last;
+    }
+    total += t.nt;
+    if (t.nt > 0) maxv = max(maxv, max(t.nt - 1 + t.c, t.last));
   }
   total = warp_sum64(total);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) maxnt = max(maxnt, __shfl_xor_sync(0xffffffffu, maxnt, o));
-  st.rounds = maxnt <= kRoundCache;
-  if (st.rounds) {
-    for (int r = lane; r <= maxnt; r += 32) st.before[r] = 0;
+  for (int o = 16; o > 0; o >>= 1) maxv = max(maxv, __shfl_xor_sync(0xffffffffu, maxv, o));
+  st.sizes = maxv <= kSizeCache;
+  if (st.sizes) {
+    int32_t* h = st.above;
+    for (int v = lane; v <= maxv + 1 && v <= kSizeCache; v += 32) h[v] = 0;
     __syncwarp();
-    for (int s = lane; s < p.num_seqs; s += 32) atomicAdd(&st.before[nt_of(p, st, s)], 1);
+    // full tiles: a range of sizes per sequence (difference array), prefix-summed below
+    for (int s = lane; s < p.num_seqs; s += 32) {
+      const SeqTiles t = seq_tiles(p, st, s);
+      if (t.nt >= 2) {
+        atomicAdd(&h[1 + t.c], 1);
+        if (t.nt + t.c <= maxv) atomicAdd(&h[t.nt + t.c], -1);
+      }
+    }
     __syncwarp();
     if (lane == 0) {
-      // histogram of tile counts -> sequences with more than r tiles -> items before r
-      int suffix = 0;
-      for (int r = maxnt; r >= 0; --r) {
-        const int h = st.before[r];
-        st.before[r] = suffix;
-        suffix += h;
+      int run = 0;
+      for (int v = 1; v <= maxv; ++v) {
+        run += h[v];
+        h[v] = run;
       }
+    }
+    __syncwarp();
+    for (int s = lane; s < p.num_seqs; s += 32) {  // last tiles: one size each
+      const SeqTiles t = seq_tiles(p, st, s);
+      if (t.nt >= 1) atomicAdd(&h[t.last], 1);
+    }
+    __syncwarp();
+    if (lane == 0) {  // histogram of sizes -> tile-items larger than v
       int acc = 0;
-      for (int r = 0; r <= maxnt; ++r) {
-        const int c = st.before[r];
-        st.before[r] = acc;
+      for (int v = maxv; v >= 1; --v) {
+        const int c = h[v];
+        h[v] = acc;
         acc += c;
       }
+      h[0] = acc;
     }
     __syncwarp();
   }
@@ -385,26 +424,44 @@ __device__ __forceinline__ int64_t build_sched_tables(const PrefillParams& p, Sc
 }
 
 // Tile-item t -> (sequence, query tile). One warp; all lanes get the result.
-__device__ __forceinline__ bool decode_tile_item(const PrefillParams& p, const SchedTables& st, int64_t t,
-                                 int maxnt, int lane, int& seq, int& tile) {
-  int lo = 0, hi = maxnt - 1;  // largest r with items_before_round(r) <= t
+__device__ __forceinline__ bool decode_tile_item(const PrefillParams& p, const SchedTables& st,
+                                                 int64_t t, int maxv, int lane, int& seq,
+                                                 int& tile) {
+  int lo = 1, hi = maxv;  // smallest v with items_above(v) <= t
   while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (items_before_round(p, st, mid, lane) <= t) lo = mid; else hi = mid - 1;
+    const int mid = (lo + hi) >> 1;
+    if (items_above(p, st, mid, lane) <= t) hi = mid; else lo = mid + 1;
   }
-  int64_t i = t - items_before_round(p, st, lo, lane);
+  const int v = lo;
+  int64_t i = t - items_above(p, st, v, lane);
   for (int base = 0; base < p.num_seqs; base += 32) {
     const int s = base + lane;
-    const int nt = s < p.num_seqs ? nt_of(p, st, s) : 0;
-    const unsigned m = __ballot_sync(0xffffffffu, nt > lo);
-    const int c = __popc(m);
-    if (i < c) {
-      const int pos = __fns(m, 0, (int)i + 1);
+    int full = 0, last = 0;
+    SeqTiles ts{0, 0, 0};
+    if (s < p.num_seqs) {
+      ts = seq_tiles(p, st, s);
+      full = (ts.nt >= 2 && v >= 1 + ts.c && v <= ts.nt - 1 + ts.c) ? 1 : 0;
+      last = (ts.nt >= 1 && ts.last == v) ? 1 : 0;
+    }
+    int incl = full + last;  // inclusive scan over the warp
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    if (i < total) {
+      const unsigned m = __ballot_sync(0xffffffffu, incl > i);
+      const int pos = __ffs(m) - 1;
+      const int before = __shfl_sync(0xffffffffu, incl - full - last, pos);
+      const int f = __shfl_sync(0xffffffffu, full, pos);
+      const int nt = __shfl_sync(0xffffffffu, ts.nt, pos);
+      const int c = __shfl_sync(0xffffffffu, ts.c, pos);
       seq = base + pos;
-      tile = __shfl_sync(0xffffffffu, nt, pos) - 1 - lo;
+      tile = (f && i - before == 0) ? v - 1 - c : nt - 1;
       return true;
     }
-    i -= c;
+    i -= total;
   }
   return false;
 }
@@ -493,10 +550,10 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
   if (warp == 0) {
     // ---------------------------------------------------------------- scheduler + producer
     SchedTables st;
-    st.nt = reinterpret_cast<int32_t*>(smem + kOffSched);
-    st.before = st.nt + kSeqCache;
-    int maxnt = 0;
-    const int64_t total = build_sched_tables(p, st, lane, maxnt);
+    st.seq = reinterpret_cast<int32_t*>(smem + kOffSched);
+    st.above = st.seq + 3 * kSeqCache;
+    int maxv = 0;
+    const int64_t total = build_sched_tables(p, st, lane, maxv);
     const int pairs = (p.group + 1) >> 1;
     const int64_t per_tile = (int64_t)(p.hq / p.group) * pairs;
     const int64_t n_items = total * per_tile;
@@ -537,7 +594,7 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
       it.seq = -1;
       if (k < n_items && !aborted) {
         int seq = 0, tile = 0;
-        if (decode_tile_item(p, st, k / per_tile, maxnt, lane, seq, tile)) {
+        if (decode_tile_item(p, st, k / per_tile, maxv, lane, seq, tile)) {
           const int r = (int)(k % per_tile);
           const int pr = r % pairs;
           it.seq = seq;
