@@ -60,8 +60,8 @@ sys.path.insert(0, str(REPO))
 # the same sequences and block tables: 616.60 MB read + 7.20 MB written.
 K2_TRAFFIC_BYTES: float | None = 623.803904e6
 # The same for K3 on the 32-prompt prefill workload, from one ncu capture of a K3 launch:
-# 240.69 MB read + 121.67 MB written.
-K3_TRAFFIC_BYTES: float | None = 362.35776e6
+# 211.81 MB read + 117.18 MB written.
+K3_TRAFFIC_BYTES: float | None = 328.994816e6
 # Prompt groups of the prefill e2e leg (copies of one group overlap another's compute).
 E2E_GROUPS = 4
 
