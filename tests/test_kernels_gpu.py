@@ -491,6 +491,43 @@ def test_prefill_running_max_jumps(ops, dtype):
     assert diff.mean().item() < BF16_MEAN, diff.mean().item()
 
 
+def test_prefill_scheduler_limits_many_prompts_and_long_history(ops):
+    """Past the scheduler's shared-memory tables (more than 1,024 sequences; a query tile
+    needing more than 1,024 KV tiles, i.e. a history past 131,072 tokens) the work items
+    are ordered from cu_seqlens and the context lengths read in global memory. Both cases
+    must still cover every query tile once: 1,100 short prompts, and a 300-token chunk
+    appended to a 140,000-token history next to two ordinary prompts."""
+    hq, hkv, d, bs = 12, 2, 128, 16
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(95)
+    cases = [
+        [int(x) for x in rng.integers(1, 40, size=1100)],
+        None,
+    ]
+    for case in cases:
+        if case is not None:
+            ctx = case
+            qlen = list(case)
+        else:
+            ctx = [140_000, 200, 77]
+            qlen = [300, 200, 77]
+        cu = np.concatenate([[0], np.cumsum(qlen)]).tolist()
+        nb = sum((c + bs - 1) // bs for c in ctx) + 2
+        kc, vc = make_pool(96, 1, nb, bs, hkv, d, torch.bfloat16)
+        tables, bt = make_tables(97, ctx, bs, nb)
+        q = torch.randn(cu[-1], hq, d, generator=torch.Generator().manual_seed(98)).to(torch.bfloat16)
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        out = torch.full((cu[-1], hq, d), float("nan"), dtype=torch.bfloat16, device=dev)
+        ops.paged_prefill(q.to(dev), kc.to(dev), vc.to(dev), 0, bt.to(dev),
+                          torch.tensor(cu, dtype=torch.int32, device=dev),
+                          torch.tensor(ctx, dtype=torch.int32, device=dev), max(qlen), bs,
+                          d ** -0.5, out=out, err_flag=err)
+        assert int(err.item()) == 0
+        assert torch.isfinite(out.float()).all()  # every row written
+        close(out, ref.prefill_attention(q, kc, vc, 0, tables, cu, ctx, bs, d ** -0.5),
+              torch.bfloat16)
+
+
 def test_prefill_trailing_slice_of_packed_batch(ops):
     """The runner's call: decode rows first, prefill rows run with views of the metadata."""
     hq, hkv, d, bs = 12, 2, 128, 16
