@@ -185,7 +185,7 @@ B2P_API int b2p_paged_decode_append(const void* q, int64_t q_tok_stride, int64_t
  *   total_q = the number of rows of q and out (>= cu_seqlens_q[num_seqs]); it bounds the
  *   grid and the TMA view of q, so no device value is read back on the host.
  *   max_q_len = the longest query run (informational).
- * bf16/f16 with head_dim 128 and block_size % 16 == 0 run on tcgen05 tensor cores
+ * bf16/f16 with head_dim 64 or 128 and block_size % 16 == 0 run on tcgen05 tensor cores
  * (TMEM accumulators); other shapes and fp32 run on CUDA cores.
  */
 B2P_API int b2p_paged_prefill(const void* q, int64_t q_tok_stride, int64_t q_head_stride,

@@ -41,7 +41,8 @@ using namespace b2p;
 
 constexpr int kM = 128;     // query rows per tile
 constexpr int kN = 128;     // keys per KV tile
-constexpr int kD = 128;     // head_dim handled by this kernel
+constexpr int kSeqCache = 1024;   // scheduler tables: sequences cached in shared memory
+constexpr int kSizeCache = 1024;  // ... and tile sizes (KV tiles per query tile)
 constexpr int kThreads = 320;
 constexpr int kSub = 16;
 constexpr int kSubPerTile = kN / kSub;
@@ -66,24 +67,27 @@ struct PrefillParams {
   int32_t* err;
 };
 
-// Shared-memory plan (bytes from the 1024-aligned base).
-constexpr int kQBytes = 2 * kM * 128;        // one head: 2 chunks x 128 rows x 128 B
-constexpr int kKVBytes = 2 * kN * 128;       // 2 chunks x 128 rows x 128 B
-constexpr int kOffQ = 0;                     // heads A and B
-constexpr int kOffK = kOffQ + 2 * kQBytes;   // 2 stages
-constexpr int kOffV = kOffK + 2 * kKVBytes;  // 2 stages
-constexpr int kOffBar = kOffV + 2 * kKVBytes;
-constexpr int kNumBars = 21;  // q_full, q_empty, k_full[2], k_empty[2], v_full[2], v_empty[2],
-                              // s_full[2], p_full[2], o_done[2] (by head), item_full[2],
-                              // item_empty[2], mma_done
-constexpr int kOffMisc = kOffBar + kNumBars * 8;
-constexpr int kOffItems = kOffMisc + 64;
-constexpr int kOffStage = (kOffItems + 2 * 48 + 127) / 128 * 128;  // epilogue: 8 warps x 32 rows x 64 B
-constexpr int kStageBytes = 32 * 64;
-constexpr int kSeqCache = 1024;
-constexpr int kSizeCache = 1024;
-constexpr int kOffSched = kOffStage + 8 * kStageBytes;  // scheduler tables
-constexpr int kSmemBytes = kOffSched + (3 * kSeqCache + kSizeCache + 1) * 4;
+// Shared-memory plan (bytes from the 1024-aligned base) for head_dim D (64 or 128): Q, K
+// and V tiles are D / 64 chunks of 128-byte lines (64 elements), 128 rows each.
+template <int D>
+struct Plan {
+  static constexpr int kChunks = D / 64;
+  static constexpr int kQBytes = kChunks * kM * 128;   // one head
+  static constexpr int kKVBytes = kChunks * kN * 128;  // one K or V tile
+  static constexpr int kOffQ = 0;                      // heads A and B
+  static constexpr int kOffK = kOffQ + 2 * kQBytes;    // 2 stages
+  static constexpr int kOffV = kOffK + 2 * kKVBytes;   // 2 stages
+  static constexpr int kOffBar = kOffV + 2 * kKVBytes;
+  static constexpr int kNumBars = 21;  // q_full, q_empty, k_full[2], k_empty[2], v_full[2],
+                                       // v_empty[2], s_full[2], p_full[2], o_done[2] (by
+                                       // head), item_full[2], item_empty[2], mma_done
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
+  static constexpr int kOffItems = kOffMisc + 64;
+  // epilogue staging: 8 warps x 32 rows x 64 B
+  static constexpr int kOffStage = (kOffItems + 2 * 48 + 127) / 128 * 128;
+  static constexpr int kOffSched = kOffStage + 8 * 32 * 64;  // scheduler tables
+  static constexpr int kSmemBytes = kOffSched + (3 * kSeqCache + kSizeCache + 1) * 4;
+};
 
 // TMEM columns (512 allocated): S of head A at 0, of head B at 128, O_A at 256, O_B at
 // 384. P overwrites the second half of its S (columns +64 .. +127, two keys per column).
@@ -470,15 +474,16 @@ __device__ __forceinline__ bool decode_tile_item(const PrefillParams& p, const S
 // (dynamic, so faster SMs take more items and the short items come last). Tensor memory,
 // barriers and descriptors are set up once; the stage and per-head counters run on across
 // items, so the next item's Q and first K/V tiles load while the current item finishes.
-template <typename T>
+template <typename T, int D>
 __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_constant__ CUtensorMap qmap,
                                                                 const __grid_constant__ CUtensorMap kmap,
                                                                 const __grid_constant__ CUtensorMap vmap,
                                                                 const PrefillParams p) {
+  using L = Plan<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
   uint64_t* q_full = bars;
   uint64_t* q_empty = bars + 1;
   uint64_t* k_full = bars + 2;       // by stage
@@ -491,10 +496,10 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
   uint64_t* item_full = bars + 16;   // by ring slot
   uint64_t* item_empty = bars + 18;
   uint64_t* mma_done = bars + 20;
-  int32_t* misc = reinterpret_cast<int32_t*>(smem + kOffMisc);
+  int32_t* misc = reinterpret_cast<int32_t*>(smem + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 5);
-  ItemInfo* items = reinterpret_cast<ItemInfo*>(smem + kOffItems);
+  ItemInfo* items = reinterpret_cast<ItemInfo*>(smem + L::kOffItems);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -550,7 +555,7 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
   if (warp == 0) {
     // ---------------------------------------------------------------- scheduler + producer
     SchedTables st;
-    st.seq = reinterpret_cast<int32_t*>(smem + kOffSched);
+    st.seq = reinterpret_cast<int32_t*>(smem + L::kOffSched);
     st.above = st.seq + 3 * kSeqCache;
     int maxv = 0;
     const int64_t total = build_sched_tables(p, st, lane, maxv);
@@ -573,12 +578,12 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
       if (gv >= 2 && !mbar_wait_bounded(&v_empty[sv], (uint32_t)(((gv >> 1) - 1) & 1), p.err))
         return false;
       if (*abort_flag) return false;
-      uint8_t* vdst = smem + kOffV + sv * kKVBytes;
-      mbar_arrive_expect_tx(&v_full[sv], kKVBytes);
+      uint8_t* vdst = smem + L::kOffV + sv * L::kKVBytes;
+      mbar_arrive_expect_tx(&v_full[sv], L::kKVBytes);
 #pragma unroll
       for (int u = 0; u < kSubPerTile; ++u)
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+        for (int c = 0; c < L::kChunks; ++c)
           tma_load_5d(vdst + c * (kN * 128) + u * (kSub * 128), &vmap, &v_full[sv], 0, c, kvh_,
                       sl[u], p.layer);
       misc[3] = (int)(gv + 1);  // V tiles issued
@@ -637,10 +642,10 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
           aborted = true;
         } else {
           const int nh = it.qh_b >= 0 ? 2 : 1;
-          mbar_arrive_expect_tx(q_full, nh * kQBytes);
+          mbar_arrive_expect_tx(q_full, nh * L::kQBytes);
           for (int h = 0; h < nh; ++h)
-            for (int c = 0; c < 2; ++c)
-              tma_load_4d(smem + kOffQ + h * kQBytes + c * (kM * 128), &qmap, q_full, 0, c,
+            for (int c = 0; c < L::kChunks; ++c)
+              tma_load_4d(smem + L::kOffQ + h * L::kQBytes + c * (kM * 128), &qmap, q_full, 0, c,
                           h ? it.qh_b : it.qh_a, it.q0 + it.qt * kM);
           misc[1] = nq + 1;  // Q loads issued
         }
@@ -679,12 +684,12 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
           } else if (*abort_flag) {
             aborted = true;
           } else {
-            uint8_t* kdst = smem + kOffK + s * kKVBytes;
-            mbar_arrive_expect_tx(&k_full[s], kKVBytes);
+            uint8_t* kdst = smem + L::kOffK + s * L::kKVBytes;
+            mbar_arrive_expect_tx(&k_full[s], L::kKVBytes);
 #pragma unroll
             for (int u = 0; u < kSubPerTile; ++u)
 #pragma unroll
-              for (int c = 0; c < 2; ++c)
+              for (int c = 0; c < L::kChunks; ++c)
                 tma_load_5d(kdst + c * (kN * 128) + u * (kSub * 128), &kmap, &k_full[s], 0, c,
                             kvh, slots[u], p.layer);
             misc[2] = (int)(g + 1);  // K tiles issued
@@ -702,7 +707,7 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     const uint32_t id_qk = idesc_f16(ab, kM, kN, 0, 0);
-    const uint32_t id_pv = idesc_f16(ab, kM, kD, 0, 1);
+    const uint32_t id_pv = idesc_f16(ab, kM, D, 0, 1);
     int64_t g = 0;
     int nq = 0;
     int n0 = 0, n1 = 0;  // PV MMAs issued for head A / head B (S, P and O barrier phases)
@@ -714,11 +719,11 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
       const int nh = it.qh_b >= 0 ? 2 : 1;
       if (lane == 0) {
         auto issue_qk = [&](int h, int64_t gg) {
-          const uint32_t q_addr = smem_u32(smem + kOffQ + h * kQBytes);
-          const uint32_t k_addr = smem_u32(smem + kOffK + (int)(gg & 1) * kKVBytes);
+          const uint32_t q_addr = smem_u32(smem + L::kOffQ + h * L::kQBytes);
+          const uint32_t k_addr = smem_u32(smem + L::kOffK + (int)(gg & 1) * L::kKVBytes);
           const uint32_t d = tbase + col_s(h);
 #pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk) {
+          for (int kk = 0; kk < D / 16; ++kk) {
             const uint64_t da = smem_desc_sw128(q_addr + (kk >> 2) * (kM * 128) + (kk & 3) * 32, 16, 1024);
             const uint64_t db = smem_desc_sw128(k_addr + (kk >> 2) * (kN * 128) + (kk & 3) * 32, 16, 1024);
             mma_ss(d, da, db, id_qk, kk > 0 ? 1u : 0u);
@@ -726,7 +731,7 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
           mma_commit(&s_full[h]);
         };
         auto issue_pv = [&](int h, int64_t gg, bool first) {
-          const uint32_t v_addr = smem_u32(smem + kOffV + (int)(gg & 1) * kKVBytes);
+          const uint32_t v_addr = smem_u32(smem + L::kOffV + (int)(gg & 1) * L::kKVBytes);
           const uint32_t p_tmem = tbase + col_s(h) + kColP;
 #pragma unroll
           for (int kk = 0; kk < kN / 16; ++kk) {
@@ -841,7 +846,7 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) return false;
           tc_fence_after();
-          for (int c0 = 0; c0 < kD; c0 += 16) {  // 16 columns at a time: S/P stay live
+          for (int c0 = 0; c0 < D; c0 += 16) {  // 16 columns at a time: S/P stay live
             uint32_t o[16];
             tmem_ld16(o_col + c0, o);
             tmem_wait_ld();
@@ -937,9 +942,9 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
         if (h == 0 && j == it.n_kv - 1 && tail0 < kN) {
           const int64_t gv = g;
           if (!mbar_wait_bounded(&v_full[gv & 1], (uint32_t)((gv >> 1) & 1), p.err)) ok = false;
-          uint8_t* vt = smem + kOffV + (int)(gv & 1) * kKVBytes;
+          uint8_t* vt = smem + L::kOffV + (int)(gv & 1) * L::kKVBytes;
           const int zrows = kN - max(tail0, 0);
-          for (int e = threadIdx.x - 64; e < 2 * zrows * 8; e += 128) {
+          for (int e = threadIdx.x - 64; e < L::kChunks * zrows * 8; e += 128) {
             const int c = e / (zrows * 8);         // d chunk
             const int rem = e - c * zrows * 8;
             const int r = max(tail0, 0) + rem / 8;  // token row
@@ -963,11 +968,11 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
         // 32 columns at a time: each thread puts its row's 64 bytes in the warp's staging
         // buffer (16-byte pieces XOR-swizzled by row), then the warp writes 8 rows x 64 B
         // per store instruction instead of 32 scattered rows.
-        uint8_t* stage = smem + kOffStage + (warp - 2) * kStageBytes;
+        uint8_t* stage = smem + L::kOffStage + (warp - 2) * (32 * 64);
         const int64_t row0 = (int64_t)it.q0 + it.qt * kM + quarter * 32;  // this warp's rows
         const int nrows = min(32, it.rows_valid - quarter * 32);
         T* obase = reinterpret_cast<T*>(p.out) + (int64_t)qh * p.o_head;
-        for (int c0 = 0; c0 < kD; c0 += 32) {
+        for (int c0 = 0; c0 < D; c0 += 32) {
           uint32_t o[32];
           tmem_ld32(o_col + c0, o);
           tmem_wait_ld();
@@ -1050,7 +1055,8 @@ int b2p_prefill_tc(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
                    int num_kv_heads, int head_dim, int block_size, float scale, void* out,
                    int64_t out_tok_stride, int64_t out_head_stride, int dtype, int32_t* err_flag,
                    void* stream) {
-  if (head_dim != kD || (dtype != B2P_BF16 && dtype != B2P_F16) || block_size % kSub != 0)
+  if ((head_dim != 64 && head_dim != 128) || (dtype != B2P_BF16 && dtype != B2P_F16) ||
+      block_size % kSub != 0)
     return B2P_EUNSUPPORTED;
   auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
   if (!al16(q) || !al16(out) || !al16(key_cache) || !al16(value_cache) ||
@@ -1103,19 +1109,24 @@ int b2p_prefill_tc(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
     const uint32_t slot = next_slot.fetch_add(1) % kCounterSlots;
     p.ctr = static_cast<int32_t*>(addr) + 2 * slot;
   }
-  const void* fn = dtype == B2P_BF16
-                       ? reinterpret_cast<const void*>(&paged_prefill_tc<__nv_bfloat16>)
-                       : reinterpret_cast<const void*>(&paged_prefill_tc<__half>);
-  const int smem = kSmemBytes + 1024;
-  // Persistent: one CTA per SM walks the work items (its 512 TMEM columns and ~222 KB of
-  // shared memory fill the SM). Once per device and element type: the kernel's
-  // shared-memory attributes, and whether one CTA fits the SM's limits.
-  static int resident[64][2] = {};
+  const bool bf16 = dtype == B2P_BF16;
+  const int variant = (bf16 ? 0 : 1) + (head_dim == 64 ? 2 : 0);
+  const void* fn =
+      head_dim == 64
+          ? (bf16 ? reinterpret_cast<const void*>(&paged_prefill_tc<__nv_bfloat16, 64>)
+                  : reinterpret_cast<const void*>(&paged_prefill_tc<__half, 64>))
+          : (bf16 ? reinterpret_cast<const void*>(&paged_prefill_tc<__nv_bfloat16, 128>)
+                  : reinterpret_cast<const void*>(&paged_prefill_tc<__half, 128>));
+  const int smem = (head_dim == 64 ? Plan<64>::kSmemBytes : Plan<128>::kSmemBytes) + 1024;
+  // Persistent: one CTA per SM walks the work items (its 512 TMEM columns and, for head_dim
+  // 128, ~222 KB of shared memory fill the SM). Once per device and kernel variant: the
+  // kernel's shared-memory attributes, and whether one CTA fits the SM's limits.
+  static int resident[64][4] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return b2p_host::record_error(e);
   if (dev < 0 || dev >= 64) return B2P_EUNSUPPORTED;
-  int& fit = resident[dev][dtype == B2P_BF16 ? 0 : 1];
+  int& fit = resident[dev][variant];
   if (fit == 0) {
     cudaFuncAttributes fa;
     int smem_sm = 0, reserved = 0, regs_sm = 0;

@@ -418,10 +418,13 @@ def test_metadata_bit_exact(ops):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_prefill_tensor_core_long_prompts_and_chunks(ops, dtype):
+@pytest.mark.parametrize("shape", [(12, 2, 128), (14, 2, 64)])
+def test_prefill_tensor_core_long_prompts_and_chunks(ops, dtype, shape):
     """Prompts up to 2,100 tokens (several 128-row tiles, many 128-key tiles), fragmented
-    blocks, whole-history and chunked runs, NaN in the pool slots past every context."""
-    hq, hkv, d, bs = 12, 2, 128, 16
+    blocks, whole-history and chunked runs, NaN in the pool slots past every context; the
+    Qwen2.5-1.5B/7B head size (128) and the Qwen2.5-0.5B one (64)."""
+    hq, hkv, d = shape
+    bs = 16
     dev = torch.device("cuda")
     rng = np.random.default_rng(80)
     ctx = [2100, 64, 129, 1000, 777, 300, 16]
