@@ -4,8 +4,8 @@
   Qwen2.5-0.5B architecture from torch.manual_seed(0), 8 requests, 32 greedy tokens each,
   block 16, pool 2048) recorded by tests/golden/make_golden.py must be reproduced token
   for token by this package's engine + B200PagedModelRunner on the GPU.
-* Logits, bf16: a 2-layer model with the Qwen2.5-1.5B attention shape (12/2 heads,
-  head_dim 128) against the reference-style packed runner (gather + dense mask + SDPA)
+* Logits, bf16: 2-layer models with the Qwen2.5-1.5B attention shape (12/2 heads,
+  head_dim 128) and the Qwen2.5-0.5B one (14/2 heads, head_dim 64) against the reference-style packed runner (gather + dense mask + SDPA)
   run in fp32 on the same weights. The bf16 error budget is that of the reference path
   itself: the same packed runner run in bf16 on the GPU sets it, and this package's logits
   must stay within 1.5x of its max-abs error (and never above 0.1); top-1 agreement on
@@ -92,30 +92,32 @@ def test_chunked_prefill_engine_reproduces_reference_tokens_fp32():
         assert got[rid] == want, (rid, got[rid], want)
 
 
-def small_1p5b_attention_model(seed=0):
+def small_1p5b_attention_model(seed=0, hidden=1536, heads=12):
     from transformers import Qwen2Config, Qwen2ForCausalLM
 
-    cfg = Qwen2Config(vocab_size=1000, hidden_size=1536, intermediate_size=512,
-                      num_hidden_layers=2, num_attention_heads=12, num_key_value_heads=2,
+    cfg = Qwen2Config(vocab_size=1000, hidden_size=hidden, intermediate_size=512,
+                      num_hidden_layers=2, num_attention_heads=heads, num_key_value_heads=2,
                       rope_theta=1_000_000.0, max_position_embeddings=4096,
                       attn_implementation="sdpa")
     torch.manual_seed(seed)
     return Qwen2ForCausalLM(cfg).eval()
 
 
-def test_bf16_runner_logits_match_reference_path():
+@pytest.mark.parametrize("hidden,heads", [(1536, 12), (896, 14)])
+def test_bf16_runner_logits_match_reference_path(hidden, heads):
     dev = torch.device("cuda")
-    base = small_1p5b_attention_model()
+    base = small_1p5b_attention_model(hidden=hidden, heads=heads)
+    d = hidden // heads  # 128 (Qwen2.5-1.5B shape) or 64 (Qwen2.5-0.5B shape)
     ref_model = copy.deepcopy(base).float()
     ours_model = copy.deepcopy(base).to(dev, torch.bfloat16)
     bs, blocks = 16, 256
-    storage = PagedKVStorage(2, blocks, bs, 2, 128, torch.bfloat16, dev)
+    storage = PagedKVStorage(2, blocks, bs, 2, d, torch.bfloat16, dev)
     runner = B200PagedModelRunner(ours_model, dev, storage)
-    kr = torch.zeros(2, blocks * bs, 2, 128)
-    vr = torch.zeros(2, blocks * bs, 2, 128)
+    kr = torch.zeros(2, blocks * bs, 2, d)
+    vr = torch.zeros(2, blocks * bs, 2, d)
     reference = ReferencePackedRunner(ref_model, kr, vr, bs)
     # the reference path itself in bf16 (GPU): its distance from fp32 is the bf16 budget
-    kb = torch.zeros(2, blocks * bs, 2, 128, dtype=torch.bfloat16, device=dev)
+    kb = torch.zeros(2, blocks * bs, 2, d, dtype=torch.bfloat16, device=dev)
     reference_bf16 = ReferencePackedRunner(copy.deepcopy(base).to(dev, torch.bfloat16), kb,
                                            torch.zeros_like(kb), bs)
     rng = np.random.default_rng(9)
