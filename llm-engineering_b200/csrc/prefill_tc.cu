@@ -78,9 +78,10 @@ struct Plan {
   static constexpr int kOffK = kOffQ + 2 * kQBytes;    // 2 stages
   static constexpr int kOffV = kOffK + 2 * kKVBytes;   // 2 stages
   static constexpr int kOffBar = kOffV + 2 * kKVBytes;
-  static constexpr int kNumBars = 21;  // q_full, q_empty, k_full[2], k_empty[2], v_full[2],
+  static constexpr int kNumBars = 23;  // q_full, q_empty, k_full[2], k_empty[2], v_full[2],
                                        // v_empty[2], s_full[2], p_full[2], o_done[2] (by
-                                       // head), item_full[2], item_empty[2], mma_done
+                                       // head), item_full[2], item_empty[2], mma_done,
+                                       // s_read[2] (by head; head_dim 64)
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kOffItems = kOffMisc + 64;
   // epilogue staging: 8 warps x 32 rows x 64 B
@@ -89,12 +90,20 @@ struct Plan {
   static constexpr int kSmemBytes = kOffSched + (3 * kSeqCache + kSizeCache + 1) * 4;
 };
 
-// TMEM columns (512 allocated): S of head A at 0, of head B at 128, O_A at 256, O_B at
-// 384. P overwrites the second half of its S (columns +64 .. +127, two keys per column).
+// TMEM columns (512 allocated): S of head A at 0, of head B at 128. head_dim 128: O_A at
+// 256, O_B at 384, and P overwrites the second half of its S (columns +64 .. +127, two keys
+// per column). head_dim 64: O_A at 256, O_B at 320, and P has columns of its own (P_A at
+// 384, P_B at 448), so S is free for the next QK^T as soon as the softmax has read it.
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColP = 64;
 __device__ __forceinline__ uint32_t col_s(int h) { return h ? 128u : 0u; }
-__device__ __forceinline__ uint32_t col_o(int h) { return h ? 384u : 256u; }
+template <int D>
+__device__ __forceinline__ uint32_t col_o(int h) {
+  return D == 64 ? 256u + 64u * h : (h ? 384u : 256u);
+}
+template <int D>
+__device__ __forceinline__ uint32_t col_p(int h) {
+  return D == 64 ? 384u + 64u * h : col_s(h) + 64u;
+}
 
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   uint64_t d = 0;
@@ -496,6 +505,7 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
   uint64_t* item_full = bars + 16;   // by ring slot
   uint64_t* item_empty = bars + 18;
   uint64_t* mma_done = bars + 20;
+  uint64_t* s_read = bars + 21;      // by head: the softmax has read S (head_dim 64)
   int32_t* misc = reinterpret_cast<int32_t*>(smem + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 5);
@@ -517,6 +527,7 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
       mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&p_full[s], kM);
+      mbar_init(&s_read[s], kM);
       mbar_init(&o_done[s], 1);
       mbar_init(&item_full[s], 1);
       mbar_init(&item_empty[s], kConsumerWarps);
@@ -732,18 +743,20 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
         };
         auto issue_pv = [&](int h, int64_t gg, bool first) {
           const uint32_t v_addr = smem_u32(smem + L::kOffV + (int)(gg & 1) * L::kKVBytes);
-          const uint32_t p_tmem = tbase + col_s(h) + kColP;
+          const uint32_t p_tmem = tbase + col_p<D>(h);
 #pragma unroll
           for (int kk = 0; kk < kN / 16; ++kk) {
             const uint64_t db = smem_desc_sw128(v_addr + kk * (16 * 128), kN * 128, 1024);
-            mma_ts(tbase + col_o(h), p_tmem + kk * 8, db, id_pv, (!first || kk > 0) ? 1u : 0u);
+            mma_ts(tbase + col_o<D>(h), p_tmem + kk * 8, db, id_pv, (!first || kk > 0) ? 1u : 0u);
           }
           mma_commit(&o_done[h]);
         };
-        // S of head h is free once the PV MMA of its previous tile has read P.
+        // S of head h is free once the PV MMA of its previous tile has read P (head_dim
+        // 128: P overwrites S), or once the softmax has read the previous S (head_dim 64).
         auto s_free = [&](int h) -> bool {
           const int n = h ? n1 : n0;
-          return n == 0 || mbar_wait_bounded(&o_done[h], (uint32_t)((n - 1) & 1), p.err);
+          return n == 0 || mbar_wait_bounded(D == 64 ? &s_read[h] : &o_done[h],
+                                             (uint32_t)((n - 1) & 1), p.err);
         };
         ok = mbar_wait_bounded(q_full, (uint32_t)(nq & 1), p.err);
         if (ok) ok = mbar_wait_bounded(&k_full[g & 1], (uint32_t)((g >> 1) & 1), p.err);
@@ -758,34 +771,66 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
           mma_commit(&k_empty[g & 1]);
           if (it.n_kv == 1) mma_commit(q_empty);  // the item's last read of Q
         }
-        for (int j = 0; j < it.n_kv && ok && !*abort_flag; ++j, ++g) {
-          const int s = (int)(g & 1);
-          const bool more = j + 1 < it.n_kv;
-          ok = mbar_wait_bounded(&v_full[s], (uint32_t)((g >> 1) & 1), p.err);
-          // PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1): each head's next S is computed while
-          // the other head's softmax runs.
-          for (int h = 0; h < nh && ok; ++h) {
-            const int n = h ? n1 : n0;
-            ok = mbar_wait_bounded(&p_full[h], (uint32_t)(n & 1), p.err);
-            if (!ok) break;
-            tc_fence_after();
-            issue_pv(h, g, j == 0);
-            if (h) ++n1; else ++n0;
-            if (more) {
-              if (h == 0)
-                ok = mbar_wait_bounded(&k_full[(g + 1) & 1], (uint32_t)(((g + 1) >> 1) & 1), p.err);
-              ok = ok && s_free(h);
+        if constexpr (D == 64) {
+          // QK_A(j+1), QK_B(j+1) as soon as each head's softmax has read S(j), then PV_A(j),
+          // PV_B(j): the next S is ready when the softmax of this tile ends.
+          for (int j = 0; j < it.n_kv && ok && !*abort_flag; ++j, ++g) {
+            const int s = (int)(g & 1);
+            if (j + 1 < it.n_kv) {
+              ok = mbar_wait_bounded(&k_full[(g + 1) & 1], (uint32_t)(((g + 1) >> 1) & 1), p.err);
+              for (int h = 0; h < nh && ok; ++h) {
+                const int n = h ? n1 : n0;
+                ok = mbar_wait_bounded(&s_read[h], (uint32_t)(n & 1), p.err);
+                if (!ok) break;
+                tc_fence_after();
+                issue_qk(h, g + 1);
+              }
+              if (!ok) break;
+              mma_commit(&k_empty[(g + 1) & 1]);
+              if (j + 2 == it.n_kv) mma_commit(q_empty);
+            }
+            ok = mbar_wait_bounded(&v_full[s], (uint32_t)((g >> 1) & 1), p.err);
+            for (int h = 0; h < nh && ok; ++h) {
+              const int n = h ? n1 : n0;
+              ok = mbar_wait_bounded(&p_full[h], (uint32_t)(n & 1), p.err);
               if (!ok) break;
               tc_fence_after();
-              issue_qk(h, g + 1);
+              issue_pv(h, g, j == 0);
+              if (h) ++n1; else ++n0;
             }
+            if (!ok) break;
+            mma_commit(&v_empty[s]);
           }
-          if (!ok) break;
-          if (more) {
-            mma_commit(&k_empty[(g + 1) & 1]);
-            if (j + 2 == it.n_kv) mma_commit(q_empty);
+        } else {
+          for (int j = 0; j < it.n_kv && ok && !*abort_flag; ++j, ++g) {
+            const int s = (int)(g & 1);
+            const bool more = j + 1 < it.n_kv;
+            ok = mbar_wait_bounded(&v_full[s], (uint32_t)((g >> 1) & 1), p.err);
+            // PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1): each head's next S is computed while
+            // the other head's softmax runs.
+            for (int h = 0; h < nh && ok; ++h) {
+              const int n = h ? n1 : n0;
+              ok = mbar_wait_bounded(&p_full[h], (uint32_t)(n & 1), p.err);
+              if (!ok) break;
+              tc_fence_after();
+              issue_pv(h, g, j == 0);
+              if (h) ++n1; else ++n0;
+              if (more) {
+                if (h == 0)
+                  ok = mbar_wait_bounded(&k_full[(g + 1) & 1], (uint32_t)(((g + 1) >> 1) & 1), p.err);
+                ok = ok && s_free(h);
+                if (!ok) break;
+                tc_fence_after();
+                issue_qk(h, g + 1);
+              }
+            }
+            if (!ok) break;
+            if (more) {
+              mma_commit(&k_empty[(g + 1) & 1]);
+              if (j + 2 == it.n_kv) mma_commit(q_empty);
+            }
+            mma_commit(&v_empty[s]);
           }
-          mma_commit(&v_empty[s]);
         }
         if (!ok) *abort_flag = 1;
       }
@@ -807,7 +852,8 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
     const int row = quarter * 32 + lane;  // query row within the tile
     const uint32_t lane_base = tbase + ((uint32_t)(quarter * 32) << 16);
     const uint32_t s_col = lane_base + col_s(h);
-    const uint32_t o_col = lane_base + col_o(h);
+    const uint32_t o_col = lane_base + col_o<D>(h);
+    const uint32_t p_col = lane_base + col_p<D>(h);
     int64_t g = 0;  // K/V tiles of the items seen so far (V stage of the tail fix-up)
     int n = 0;      // tiles of this head so far (S, P and O barrier phases)
     bool ok = true;
@@ -867,6 +913,24 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
           const float mx = whole ? row_max64<false>(r0, r1, nv) : row_max64<true>(r0, r1, nv);
           return mx * p.scale_log2 - m;
         };
+        // head_dim 64 (P has its own columns): the whole S is in registers, so the MMA warp
+        // may overwrite it with the next tile's QK^T; and P may only be stored once the
+        // previous tile's PV has read the P before it.
+        auto s_done = [&]() {
+          if constexpr (D == 64) {
+            tc_fence_before();
+            mbar_arrive(&s_read[h]);
+          }
+        };
+        auto p_writable = [&]() -> bool {
+          if constexpr (D == 64) {
+            if (n > 0 && ok && !mbar_wait_bounded(&o_done[h], (uint32_t)((n - 1) & 1), p.err))
+              ok = false;
+            ok = __all_sync(0xffffffffu, ok);
+            if (ok) tc_fence_after();
+          }
+          return ok;
+        };
         if (j == 0) {
           // First tile of the item: the reference max comes from the tile (two passes; keys
           // 64..127 are left in registers, their columns then take their P).
@@ -880,10 +944,12 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
           mx = fmaxf(mx, whole1 ? row_max64<false>(r0, r1, nv1) : row_max64<true>(r0, r1, nv1));
           m = mx * p.scale_log2;  // scale_log2 > 0 keeps the arg-max; -inf for empty rows
           rs1 = exp_half(whole1, nv1);
-          tmem_st32(s_col + kColP + 32, pk);
+          if (!p_writable()) break;
+          tmem_st32(p_col + 32, pk);
           tmem_ld32(s_col, r0);
           tmem_ld32(s_col + 32, r1);
           tmem_wait_ld();
+          s_done();
           rs0 = exp_half(whole0, nv0);
         } else {
           // Later tiles: one pass per half with the running reference m. exp2(x - m) is
@@ -906,10 +972,12 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
               rs1 = exp_half(whole1, nv1);
             }
           }
-          tmem_st32(s_col + kColP + 32, pk);
+          if (!p_writable()) break;
+          tmem_st32(p_col + 32, pk);
           tmem_ld32(s_col, r0);
           tmem_ld32(s_col + 32, r1);
           tmem_wait_ld();
+          s_done();
           rs0 = exp_half(whole0, nv0);
           if (__any_sync(0xffffffffu, !(rs0 <= kSumCheck))) {
             const float xm = xmax_half(whole0, nv0);
@@ -922,17 +990,17 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
               tmem_wait_st();
               for (int c0 = 0; c0 < 32; c0 += 16) {
                 uint32_t pv[16];
-                tmem_ld16(s_col + kColP + 32 + c0, pv);
+                tmem_ld16(p_col + 32 + c0, pv);
                 tmem_wait_ld();
 #pragma unroll
                 for (int c = 0; c < 16; ++c) pv[c] = scale_pair<T>(pv[c], alpha);
-                tmem_st16(s_col + kColP + 32 + c0, pv);
+                tmem_st16(p_col + 32 + c0, pv);
               }
               rs0 = exp_half(whole0, nv0);
             }
           }
         }
-        tmem_st32(s_col + kColP, pk);
+        tmem_st32(p_col, pk);
         l += rs1 + rs0;
         tmem_wait_st();
         // Keys past the context (the last KV tile's tail) may hold NaN/Inf in the pool;
