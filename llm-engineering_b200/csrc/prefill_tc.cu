@@ -10,21 +10,25 @@
 //   S = Q K^T   tcgen05.mma kind::f16, A = Q (smem, K-major), B = K tile (smem, K-major),
 //               D = S in tensor memory (fp32, 128 lanes x 128 columns, one per head)
 //   P = softmax rows of S, one thread per query row (tcgen05.ld -> fp32 -> exp2), written
-//       back as bf16/f16 over the second half of its own S columns (tcgen05.st)
+//       back as bf16/f16 (tcgen05.st) over the second half of its own S columns (head_dim
+//       128) or into columns of its own (head_dim 64)
 //   O += P V    tcgen05.mma with A = P from tensor memory, B = V tile (smem, MN-major),
 //               D = O in tensor memory (fp32, 128 x head_dim, one per head)
 //
 // Tensor memory holds S_A, S_B, O_A, O_B (512 columns, one CTA per SM). The MMA warp
 // issues PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1), ..., so the softmax of one head runs
 // while the tensor cores work on the other head, and both heads read each K/V tile once.
+// With head_dim 64 the order is QK_A(j+1), QK_B(j+1), PV_A(j), PV_B(j): P has columns of
+// its own there, so the next QK^T only waits for the softmax to have read S.
 // K/V tiles of 128 tokens are assembled from eight 16-slot pool sub-blocks (TMA tile
 // loads, 128-byte swizzle, no multicast) into two-stage K and V rings. A query row j of
 // sequence i sits at position ctx_i - q_len_i + j and sees keys 0..position (whole-history
 // prefill when q_len == ctx, chunked prefill otherwise). The first KV tile of an item sets
 // each row's reference max; later tiles take exp2 against that reference in one pass (the
 // row sum flags the rare rows whose scores outgrow it by more than 2^8, which then move
-// the reference and rescale O, l and the P already stored). The softmax is bound by FP32
-// instruction issue, so the exponent arithmetic runs as packed f32x2 FMA/ADD.
+// the reference and rescale O, l and the P already stored). The softmax is bound by
+// latency (tensor-memory round trips and its per-thread chain) more than by exp2
+// throughput; the exponent arithmetic runs as packed f32x2 FMA/ADD.
 //
 // Warp roles (320 threads): warp 0 = TMA producer and work-item scheduler, warp 1 =
 // tensor-memory owner and MMA issuer (one thread), warps 2..5 = softmax + epilogue of head
