@@ -27,8 +27,8 @@
 // each row's reference max; later tiles take exp2 against that reference in one pass (the
 // row sum flags the rare rows whose scores outgrow it by more than 2^8, which then move
 // the reference and rescale O, l and the P already stored). The softmax is bound by
-// latency (tensor-memory round trips and its per-thread chain) more than by exp2
-// throughput; the exponent arithmetic runs as packed f32x2 FMA/ADD.
+// neither exp2 throughput nor its tensor-memory loads but is sensitive to issue slots on
+// its SM sub-partition, so the exponent arithmetic runs as packed f32x2 FMA/ADD.
 //
 // Warp roles (320 threads): warp 0 = TMA producer and work-item scheduler, warp 1 =
 // tensor-memory owner and MMA issuer (one thread), warps 2..5 = softmax + epilogue of head
