@@ -191,6 +191,66 @@ def make_workload(seed: int, device: torch.device | None, layers: int = 1):
     }
 
 
+LC_SEQS = 64
+LC_CTX_LO, LC_CTX_HI = 8192, 32768
+LC_HQ, LC_HKV = 28, 4
+LC_CHURN = 0.3
+
+
+def longctx_tables(seed: int):
+    """Block tables of the long-context configuration after seeded alloc/free churn, made
+    with the engine's own FIFO block pool: the 64 sequences grow together one block at a
+    time (continuous batching), then 30% of all allocated blocks are freed in random order
+    (they rejoin the free queue's tail) and each freed position is allocated again from
+    the queue's head, so every table mixes runs of first-use and recycled blocks."""
+    import __graft_entry__ as entry
+
+    entry.load_package()
+    from llm_engineering_b200.engine.block import BlockPool
+
+    rng = np.random.default_rng(seed)
+    ctx = rng.integers(LC_CTX_LO, LC_CTX_HI + 1, size=LC_SEQS).astype(np.int32)
+    need = (ctx + BLOCK_SIZE - 1) // BLOCK_SIZE
+    num_blocks = int(need.sum() * 1.05) + 64
+    pool = BlockPool(num_blocks)
+    tables: list[list[int]] = [[] for _ in range(LC_SEQS)]
+    for step in range(int(need.max())):
+        for i in range(LC_SEQS):
+            if step < need[i]:
+                tables[i].append(pool.allocate(1)[0])
+    taken = [(i, j) for i in range(LC_SEQS) for j in range(int(need[i]))]
+    victims = [taken[k] for k in rng.permutation(len(taken))[: int(LC_CHURN * len(taken))]]
+    for i, j in victims:
+        pool.free(tables[i][j])
+    for i, j in victims:
+        tables[i][j] = pool.allocate(1)[0]
+    return ctx, tables, num_blocks
+
+
+def make_longctx_workload(seed: int, device: torch.device, layers: int = 1):
+    """Seeded long-context decode batch (Qwen2.5-7B attention shape: 28 Q / 4 KV heads,
+    head_dim 128) over a churned pool: K/V pool drawn N(0,1) per layer on `device`, and
+    per layer the query rows and each sequence's newest K/V row."""
+    ctx, tables, num_blocks = longctx_tables(seed)
+    width = int(max(len(t) for t in tables))
+    bt = np.full((LC_SEQS, width), -1, dtype=np.int32)
+    for i, t in enumerate(tables):
+        bt[i, :len(t)] = t
+    gd = torch.Generator(device=device).manual_seed(seed)
+    shape = (layers, num_blocks * BLOCK_SIZE, LC_HKV, HEAD_DIM)
+    kc = torch.empty(shape, dtype=torch.bfloat16, device=device)
+    vc = torch.empty(shape, dtype=torch.bfloat16, device=device)
+    for layer in range(layers):
+        kc[layer] = torch.randn(shape[1:], generator=gd, device=device)
+        vc[layer] = torch.randn(shape[1:], generator=gd, device=device)
+    q = torch.randn(layers, LC_SEQS, LC_HQ, HEAD_DIM, generator=gd, device=device)
+    new_k = torch.randn(layers, LC_SEQS, LC_HKV, HEAD_DIM, generator=gd, device=device)
+    new_v = torch.randn(layers, LC_SEQS, LC_HKV, HEAD_DIM, generator=gd, device=device)
+    return {"ctx": ctx, "tables": bt, "table_lists": tables, "kc": kc, "vc": vc,
+            "q": q.to(torch.bfloat16), "new_k": new_k.to(torch.bfloat16),
+            "new_v": new_v.to(torch.bfloat16)}
+
+
 def algorithmic_bytes(ctx: np.ndarray) -> float:
     kv = 2 * HKV * HEAD_DIM * 2 * float(ctx.sum())          # K + V rows read
     qo = 2 * NUM_SEQS * HQ * HEAD_DIM * 2                   # Q read + O written

@@ -73,6 +73,26 @@ B2P_API int b2p_last_cuda_error(void);
 B2P_API const char* b2p_status_string(int status);
 
 /*
+ * bf16/f16 launches of kernel 2 (b2p_paged_decode / _append / _noalloc) or kernel 3
+ * (b2p_paged_prefill) since the library was loaded that ran on the CUDA-core kernels
+ * because the tensor-core kernel's preconditions were not met (block_size not a multiple
+ * of 16, unsupported head_dim or GQA group, unaligned rows or strides). Such a call
+ * still returns B2P_OK with correct results, but runs many times slower; fp32 calls,
+ * which always take the CUDA-core kernels, are not counted. Returns -1 for another
+ * kernel number. No counterpart in the reference (its PyTorch path has one route).
+ */
+B2P_API int64_t b2p_cuda_core_fallbacks(int kernel);
+
+/*
+ * Zero, on `stream`, the device-resident claim counters of b2p_paged_prefill on the
+ * current device. Every prefill launch that runs to its end leaves its counters zeroed;
+ * call this after a launch reported B2P_DEV_WAIT_TIMEOUT (its counters may then be left
+ * set), with no prefill launch in flight. (The decode workspace is the caller's: zero it
+ * with a memset in that case.) No counterpart in the reference.
+ */
+B2P_API int b2p_reset_scratch(void* stream);
+
+/*
  * K1 — KV-cache write.
  * Replaces PagedKVStorage.scatter (serving/engine/paged_kv_storage.py:76-136), i.e. the
  * two index_copy_ calls at :135-136, for a whole packed batch in one launch: row t of
@@ -132,8 +152,9 @@ B2P_API int b2p_paged_decode(const void* q, int64_t q_tok_stride, int64_t q_head
  *     current); make that first call before any stream capture.
  *   - Every call clears the counters on `stream` and reuses the same array, so calls whose
  *     work overlaps on the GPU (other streams, other threads) race: serialise them.
- *   - Returns B2P_EWORKSPACE, launching nothing, when the problem needs more than the
- *     array holds.
+ *   - Checks every argument, and the scratch the chosen kernel needs against the array's
+ *     size, before it queues anything: a call that returns an error (B2P_EWORKSPACE when
+ *     the problem needs more than the array holds) has queued no work on `stream`.
  *   - Allocates nothing (no cudaMalloc / cudaFree).
  */
 B2P_API int b2p_paged_decode_noalloc(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
@@ -186,7 +207,14 @@ B2P_API int b2p_paged_decode_append(const void* q, int64_t q_tok_stride, int64_t
  *   grid and the TMA view of q, so no device value is read back on the host.
  *   max_q_len = the longest query run (informational).
  * bf16/f16 with head_dim 64 or 128 and block_size % 16 == 0 run on tcgen05 tensor cores
- * (TMEM accumulators); other shapes and fp32 run on CUDA cores.
+ * (TMEM accumulators); other shapes and fp32 run on CUDA cores (counted by
+ * b2p_cuda_core_fallbacks(3) for bf16/f16).
+ * Each tensor-core launch takes one of 64 device-resident claim-counter slots, round
+ * robin, and leaves it zeroed when it ends: at most 64 prefill launches may be in flight
+ * on one device at a time (streams and threads together). A launch captured into a CUDA
+ * graph keeps the slot it drew at capture, so replays of that graph must not overlap, on
+ * the GPU, with other prefill launches (the 64th launch after it draws the same slot):
+ * replay it on the stream the other prefill launches use.
  */
 B2P_API int b2p_paged_prefill(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
                       const void* key_cache, const void* value_cache, int64_t layer_index,

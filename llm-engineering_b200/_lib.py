@@ -33,6 +33,8 @@ EXPORTED_SYMBOLS = (
     "b2p_version",
     "b2p_last_cuda_error",
     "b2p_status_string",
+    "b2p_cuda_core_fallbacks",
+    "b2p_reset_scratch",
     "b2p_kv_write",
     "b2p_paged_decode_workspace_size",
     "b2p_paged_decode",
@@ -55,6 +57,8 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "b2p_version": (_i32, []),
     "b2p_last_cuda_error": (_i32, []),
     "b2p_status_string": (ctypes.c_char_p, [_i32]),
+    "b2p_cuda_core_fallbacks": (_i64, [_i32]),
+    "b2p_reset_scratch": (_i32, [_p]),
     "b2p_kv_write": (
         _i32,
         [_p, _i64, _i64, _p, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _i32, _i32,

@@ -3,13 +3,19 @@
 // KV pool tensors.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
 
+int b2p_prefill_reset_counters(void* stream);  // prefill_tc.cu
+
 namespace {
 
 thread_local int g_last_cuda_error = 0;
+
+// bf16/f16 launches that ran on the CUDA-core kernels, per kernel (index 2: K2, 3: K3).
+std::atomic<int64_t> g_fallbacks[4];
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -109,6 +115,10 @@ int record_error(cudaError_t e) {
   return B2P_ELAUNCH;
 }
 
+void note_fallback(int kernel) {
+  if (kernel >= 0 && kernel < 4) g_fallbacks[kernel].fetch_add(1, std::memory_order_relaxed);
+}
+
 int sm_count() {
   static int counts[64] = {0};
   int dev = 0;
@@ -196,6 +206,13 @@ extern "C" {
 int b2p_version(void) { return 100; }
 
 int b2p_last_cuda_error(void) { return g_last_cuda_error; }
+
+int b2p_reset_scratch(void* stream) { return b2p_prefill_reset_counters(stream); }
+
+int64_t b2p_cuda_core_fallbacks(int kernel) {
+  if (kernel != 2 && kernel != 3) return -1;
+  return g_fallbacks[kernel].load(std::memory_order_relaxed);
+}
 
 const char* b2p_status_string(int status) {
   switch (status) {

@@ -219,11 +219,20 @@ int record_error(cudaError_t e);
 // Streaming-multiprocessor count of the current device (cached per device).
 int sm_count();
 
+// Count one bf16/f16 launch of kernel 2 (decode) or 3 (prefill) that ran on the CUDA-core
+// kernel because the tensor-core kernel's preconditions were not met.
+void note_fallback(int kernel);
+
 // Encode a 5-D tiled tensor map over one of the pool tensors
 // [num_layers, num_slots, num_kv_heads, head_dim] with the box
 // {64 elements, head_dim/64 chunks, 1 head, 16 slots, 1 layer} and 128-byte swizzle.
 // Returns B2P_OK or B2P_EDRIVER. Results are cached per (pointer, shape).
 int pool_tensor_map(CUtensorMap* out, const void* base, int64_t num_layers, int64_t num_slots,
                     int num_kv_heads, int head_dim, int elem_bytes);
+
+// The same map with a box of box_chunks 128-byte lines per slot (1: one 64-column chunk of
+// a bf16/f16 row per slot, so a 16-slot box is 16 consecutive swizzle lines).
+int pool_tensor_map_box(CUtensorMap* out, const void* base, int64_t num_layers, int64_t num_slots,
+                        int num_kv_heads, int head_dim, int elem_bytes, int box_chunks);
 
 }  // namespace b2p_host

@@ -26,9 +26,10 @@
 //    ldmatrix.trans, P^T transposed in registers with movmatrix). Each KV tile read from
 //    shared memory serves all G query heads of its group.
 //  * A sequence that lies inside one warp's range is finished from registers. A sequence
-//    cut by range boundaries leaves an fp32 partial (O, running max, running sum) per warp
-//    in the workspace; once a warp's stream is done it counts its partials in (atomic
-//    counter per sequence) and the last warp to report a sequence merges its partials.
+//    cut by range boundaries leaves a partial per warp in the workspace (O / l scaled into
+//    [-1, 1] in fp16, with the running max, running sum and scale in fp32); once a warp's
+//    stream is done it counts its partials in (atomic counter per sequence) and the last
+//    warp to report a sequence merges its partials.
 #include <mutex>
 
 #include "common.cuh"
@@ -72,14 +73,17 @@ struct DecodeParams {
 
 template <int D, int NT>
 struct Record {
-  // Partial of one (unit, sequence): O^T / l in fp16, in MMA fragment order
-  // ([D/16][NT][32 lanes][4 halves] = one 8-byte access per lane), then the running max
-  // and sum per query head in fp32. Normalised values are bounded by max|v|, so fp16
-  // keeps ~3 decimal digits; the merge re-weights them with the exact fp32 sums.
+  // Partial of one (unit, sequence): O^T / (l * s) in fp16, in MMA fragment order
+  // ([D/16][NT][32 lanes][4 halves] = one 8-byte access per lane), then per query head in
+  // fp32 the running max, the running sum and the scale s = max_d |O / l|. Normalised
+  // values are bounded by max|v|, which a bf16 pool can push far past fp16's 65504; divided
+  // by s they lie in [-1, 1], so fp16 keeps its 11-bit precision relative to the head's
+  // largest value at any magnitude. The merge re-weights them with the fp32 sums and scales.
   static constexpr int kOBytes = (D / 16) * NT * 32 * 8;
-  static constexpr int kFloats = kOBytes / 4 + 2 * NT * 8;
-  static constexpr int kM = kOBytes / 4;       // float index of the maxima
+  static constexpr int kFloats = kOBytes / 4 + 3 * NT * 8;
+  static constexpr int kM = kOBytes / 4;           // float index of the maxima
   static constexpr int kL = kOBytes / 4 + NT * 8;  // float index of the sums
+  static constexpr int kS = kOBytes / 4 + 2 * NT * 8;  // float index of the scales
 };
 
 struct Range {
@@ -249,6 +253,12 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
                                                           const DecodeParams p) {
   constexpr int kTileBytes = kSub * D * 2;  // one K or V sub-block of one head
   constexpr int kStageBytes = 2 * kTileBytes;
+  // A tile is stored as D/64 chunks of [16 tokens][64 elements] (one TMA box each), so the
+  // 8 token rows that one ldmatrix phase reads are 8 consecutive 128-byte lines: their
+  // 128-byte swizzle phases all differ and the reads are free of bank conflicts (with
+  // 256-byte token rows, rows t and t + 4 would share a phase).
+  constexpr int kChunks = D / 64;
+  constexpr int kChunkBytes = kSub * 128;
   using Rec = Record<D, NT>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -328,8 +338,12 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
       const int c3 = (int)(slot < 0 ? num_slots : slot);
       stage_slot[stage] = c3;
       mbar_arrive_expect_tx(&full[stage], kStageBytes);
-      tma_load_5d(kdst, &kmap, &full[stage], 0, 0, head, c3, p.layer);
-      tma_load_5d(kdst + kTileBytes, &vmap, &full[stage], 0, 0, head, c3, p.layer);
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        tma_load_5d(kdst + c * kChunkBytes, &kmap, &full[stage], 0, c, head, c3, p.layer);
+        tma_load_5d(kdst + kTileBytes + c * kChunkBytes, &vmap, &full[stage], 0, c, head, c3,
+                    p.layer);
+      }
     }
     issued = k + 1;
   };
@@ -438,11 +452,15 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
       const int valid = min(kSub, ctx - lb * kSub);
       if (valid < kSub) {
         // Slots past the context may hold anything (the pool is not cleared), and
-        // 0 * NaN would poison O: zero the V rows of masked tokens. A token row is
-        // D*2 contiguous bytes (whole swizzle lines), so no swizzle math is needed.
-        const int zero_bytes = (kSub - valid) * D * 2;
-        uint4* z = reinterpret_cast<uint4*>(vtile + valid * D * 2);
-        for (int i = lane; i < zero_bytes / 16; i += 32) z[i] = make_uint4(0, 0, 0, 0);
+        // 0 * NaN would poison O: zero the V rows of masked tokens. In each 64-column chunk
+        // a token is one whole 128-byte swizzle line, so no swizzle math is needed.
+        const int per_chunk = (kSub - valid) * 8;  // 16-byte pieces per chunk
+        for (int i = lane; i < kChunks * per_chunk; i += 32) {
+          const int c = i / per_chunk;
+          const int j = i - c * per_chunk;
+          reinterpret_cast<uint4*>(vtile + c * kChunkBytes + valid * 128)[j] =
+              make_uint4(0, 0, 0, 0);
+        }
         __syncwarp();
       }
       const bool patched = appends && lb == nb - 1;
@@ -461,7 +479,7 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
                                 isv ? p.new_v + ((int64_t)seq * p.nv_tok + (int64_t)head * p.nv_head) * 2
                                     : p.new_k + ((int64_t)seq * p.nk_tok + (int64_t)head * p.nk_head) * 2) + cc);
           const int d = cc * 8;
-          const uint32_t off = (uint32_t)((rrow * (D / 64) + d / 64) * 128 + (d % 64) * 2);
+          const uint32_t off = (uint32_t)(((d / 64) * kSub + rrow) * 128 + (d % 64) * 2);
           *reinterpret_cast<uint4*>((isv ? vtile : ktile) + swz128(off)) = val;
           if (in_pool) {
             uint8_t* pool = isv ? p.vpool : p.kpool;
@@ -489,7 +507,7 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const int dcol = kk * 16 + dsub;
-          const uint32_t off = (uint32_t)((tok * (D / 64) + dcol / 64) * 128 + (dcol % 64) * 2);
+          const uint32_t off = (uint32_t)(((dcol / 64) * kSub + tok) * 128 + (dcol % 64) * 2);
           uint32_t a0, a1, a2, a3;
           ldmatrix_x4(kbase + swz128(off), a0, a1, a2, a3);
 #pragma unroll
@@ -544,7 +562,7 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
 #pragma unroll
         for (int i = 0; i < D / 16; ++i) {
           const int dcol = i * 16 + dsub;
-          const uint32_t off = (uint32_t)((tok * (D / 64) + dcol / 64) * 128 + (dcol % 64) * 2);
+          const uint32_t off = (uint32_t)(((dcol / 64) * kSub + tok) * 128 + (dcol % 64) * 2);
           uint32_t a0, a1, a2, a3;
           ldmatrix_x4_trans(vbase + swz128(off), a0, a1, a2, a3);
 #pragma unroll
@@ -575,14 +593,31 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
     } else {
       const int slot_idx = (cb + lb0 == r.begin) ? 0 : 1;  // first segment of this unit or not
       float* rec = p.partials + (((size_t)head * parts + unit) * 2 + slot_idx) * Rec::kFloats;
+      float sc[NT][2];  // per query head: max_d |O / l|
 #pragma unroll
       for (int nn = 0; nn < NT; ++nn) {
-        const float i0 = l_run[nn][0] > 0.f ? 1.f / l_run[nn][0] : 0.f;
-        const float i1 = l_run[nn][1] > 0.f ? 1.f / l_run[nn][1] : 0.f;
+        float a0 = 0.f, a1 = 0.f;
 #pragma unroll
         for (int i = 0; i < D / 16; ++i) {
-          __half2 lo = __floats2half2_rn(acc[i][nn][0] * i0, acc[i][nn][1] * i1);
-          __half2 hi = __floats2half2_rn(acc[i][nn][2] * i0, acc[i][nn][3] * i1);
+          a0 = fmaxf(a0, fmaxf(fabsf(acc[i][nn][0]), fabsf(acc[i][nn][2])));
+          a1 = fmaxf(a1, fmaxf(fabsf(acc[i][nn][1]), fabsf(acc[i][nn][3])));
+        }
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {  // the 8 lanes holding one query head's rows
+          a0 = fmaxf(a0, __shfl_xor_sync(0xffffffffu, a0, o));
+          a1 = fmaxf(a1, __shfl_xor_sync(0xffffffffu, a1, o));
+        }
+        const float i0 = l_run[nn][0] > 0.f ? 1.f / l_run[nn][0] : 0.f;
+        const float i1 = l_run[nn][1] > 0.f ? 1.f / l_run[nn][1] : 0.f;
+        sc[nn][0] = a0 * i0;
+        sc[nn][1] = a1 * i1;
+        // O / l / s = O / max_d |O|: every stored value lies in [-1, 1].
+        const float f0 = a0 > 0.f ? 1.f / a0 : 0.f;
+        const float f1 = a1 > 0.f ? 1.f / a1 : 0.f;
+#pragma unroll
+        for (int i = 0; i < D / 16; ++i) {
+          __half2 lo = __floats2half2_rn(acc[i][nn][0] * f0, acc[i][nn][1] * f1);
+          __half2 hi = __floats2half2_rn(acc[i][nn][2] * f0, acc[i][nn][3] * f1);
           uint2 v;
           v.x = *reinterpret_cast<uint32_t*>(&lo);
           v.y = *reinterpret_cast<uint32_t*>(&hi);
@@ -596,6 +631,8 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
           rec[Rec::kM + nn * 8 + 2 * t4 + 1] = m_run[nn][1];
           rec[Rec::kL + nn * 8 + 2 * t4] = l_run[nn][0];
           rec[Rec::kL + nn * 8 + 2 * t4 + 1] = l_run[nn][1];
+          rec[Rec::kS + nn * 8 + 2 * t4] = sc[nn][0];
+          rec[Rec::kS + nn * 8 + 2 * t4 + 1] = sc[nn][1];
         }
       }
       // The counter update (which needs a fence) and the possible merge wait until this
@@ -660,7 +697,7 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
     // One online pass; four contributors' loads are issued before any of them is used.
     constexpr int kBatch = 4;
     for (int64_t u0 = u_first; u0 <= u_last; u0 += kBatch) {
-      float mv[kBatch][NT][2], lv[kBatch][NT][2];
+      float mv[kBatch][NT][2], lv[kBatch][NT][2], sv[kBatch][NT][2];
       uint2 ov[kBatch][D / 16][NT];
 #pragma unroll
       for (int b = 0; b < kBatch; ++b) {
@@ -675,6 +712,8 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
           mv[b][nn][1] = have ? __ldcg(pr + Rec::kM + nn * 8 + 2 * t4 + 1) : -INFINITY;
           lv[b][nn][0] = have ? __ldcg(pr + Rec::kL + nn * 8 + 2 * t4) : 0.f;
           lv[b][nn][1] = have ? __ldcg(pr + Rec::kL + nn * 8 + 2 * t4 + 1) : 0.f;
+          sv[b][nn][0] = have ? __ldcg(pr + Rec::kS + nn * 8 + 2 * t4) : 0.f;
+          sv[b][nn][1] = have ? __ldcg(pr + Rec::kS + nn * 8 + 2 * t4 + 1) : 0.f;
 #pragma unroll
           for (int i = 0; i < D / 16; ++i)
             ov[b][i][nn] = have ? __ldcg(reinterpret_cast<const uint2*>(pr) + (i * NT + nn) * 32 + lane)
@@ -693,6 +732,7 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
             w[cc] = mn == -INFINITY ? 0.f : fast_exp2(mv[b][nn][cc] - mn) * lv[b][nn][cc];
             L[nn][cc] = L[nn][cc] * a[cc] + w[cc];
             M[nn][cc] = mn;
+            w[cc] *= sv[b][nn][cc];  // stored values are O / (l * s)
           }
 #pragma unroll
           for (int i = 0; i < D / 16; ++i) {
@@ -887,6 +927,57 @@ __global__ void append_rows_by_table(AppendRows rows, uint8_t* kpool, uint8_t* v
   }
 }
 
+// How a decode call runs: validated arguments, the kernel chosen, and for the tensor-core
+// kernel the plan and the workspace bytes it needs. Shared by every decode entry point so
+// that argument and size checks all happen before anything is queued on the stream.
+struct DecodeRoute {
+  bool empty = false;  // num_seqs == 0: nothing to launch
+  bool tc = false;     // tensor-core kernel (else the CUDA-core kernel)
+  Plan pl;
+  int hpu = 1;
+  int64_t ctas = 0;
+  size_t need = 0;  // workspace bytes of the tensor-core kernel
+};
+
+int decode_route(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
+                 const void* key_cache, const void* value_cache, int64_t layer_index,
+                 int64_t num_layers, int64_t num_slots, const int32_t* block_tables,
+                 const int32_t* context_lens, int num_seqs, int num_q_heads, int num_kv_heads,
+                 int head_dim, int block_size, const void* out, int dtype, DecodeRoute& rt,
+                 size_t workspace_limit = SIZE_MAX) {
+  if (num_seqs < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 ||
+      block_size <= 0 || num_slots <= 0 || num_layers <= 0)
+    return B2P_EINVAL;
+  if (num_q_heads % num_kv_heads != 0) return B2P_EINVAL;
+  if (layer_index < 0 || layer_index >= num_layers) return B2P_ERANGE;
+  if (num_slots % block_size != 0) return B2P_EINVAL;
+  if (dtype < B2P_BF16 || dtype > B2P_F32) return B2P_EINVAL;
+  if (num_seqs == 0) {
+    rt.empty = true;
+    return B2P_OK;
+  }
+  if (!q || !key_cache || !value_cache || !block_tables || !context_lens || !out)
+    return B2P_EINVAL;
+  const int group = num_q_heads / num_kv_heads;
+  rt.tc = (dtype == B2P_BF16 || dtype == B2P_F16) && block_size % 16 == 0 &&
+          (q_tok_stride % 2 == 0) && (q_head_stride % 2 == 0) &&
+          ((reinterpret_cast<uintptr_t>(q) & 3u) == 0) &&
+          ((reinterpret_cast<uintptr_t>(key_cache) & 15u) == 0) &&
+          ((reinterpret_cast<uintptr_t>(value_cache) & 15u) == 0) &&
+          num_slots <= 0x7fffffffLL && select_plan(dtype, head_dim, group, rt.pl);
+  if (!rt.tc) return B2P_OK;
+  // The per-sequence counters alone bound the workspace from below (checked before any
+  // device query, so an oversized problem is refused without touching the GPU).
+  if (counters_bytes(num_seqs, num_kv_heads) > workspace_limit) return B2P_EWORKSPACE;
+  const int rc = prepare(rt.pl);
+  if (rc != B2P_OK) return rc;
+  rt.hpu = heads_per_unit(num_kv_heads, rt.pl.warps);
+  rt.ctas = ctas_x(rt.pl.ctas_per_sm, num_kv_heads, rt.hpu);
+  rt.need = workspace_bytes(num_seqs, num_kv_heads, rt.ctas * (rt.pl.warps / rt.hpu),
+                            rt.pl.record);
+  return B2P_OK;
+}
+
 int decode_impl(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
                 const void* key_cache, const void* value_cache, int64_t layer_index,
                 int64_t num_layers, int64_t num_slots, const int32_t* block_tables,
@@ -895,28 +986,20 @@ int decode_impl(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
                 void* out, int64_t out_tok_stride, int64_t out_head_stride, void* workspace,
                 size_t workspace_size, int dtype, int32_t* err_flag, void* stream,
                 const AppendRows& app) {
-  if (num_seqs < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 ||
-      block_size <= 0 || num_slots <= 0 || num_layers <= 0)
-    return B2P_EINVAL;
-  if (num_q_heads % num_kv_heads != 0) return B2P_EINVAL;
-  if (layer_index < 0 || layer_index >= num_layers) return B2P_ERANGE;
-  if (num_slots % block_size != 0) return B2P_EINVAL;
-  if (num_seqs == 0) return B2P_OK;
-  if (!q || !key_cache || !value_cache || !block_tables || !context_lens || !out)
-    return B2P_EINVAL;
+  DecodeRoute rt;
+  int rc = decode_route(q, q_tok_stride, q_head_stride, key_cache, value_cache, layer_index,
+                        num_layers, num_slots, block_tables, context_lens, num_seqs,
+                        num_q_heads, num_kv_heads, head_dim, block_size, out, dtype, rt);
+  if (rc != B2P_OK || rt.empty) return rc;
   const int group = num_q_heads / num_kv_heads;
-
-  Plan pl;
-  const bool tc = (dtype == B2P_BF16 || dtype == B2P_F16) && block_size % 16 == 0 &&
-                  (q_tok_stride % 2 == 0) && (q_head_stride % 2 == 0) &&
-                  ((reinterpret_cast<uintptr_t>(q) & 3u) == 0) &&
-                  ((reinterpret_cast<uintptr_t>(key_cache) & 15u) == 0) &&
-                  ((reinterpret_cast<uintptr_t>(value_cache) & 15u) == 0) &&
-                  num_slots <= 0x7fffffffLL && select_plan(dtype, head_dim, group, pl);
+  const bool tc = rt.tc;
+  // A bf16/f16 call that misses the tensor-core kernel's preconditions (block size, GQA
+  // group, head_dim, alignment) runs on CUDA cores at a fraction of the speed: count it.
+  if (!tc && dtype != B2P_F32) b2p_host::note_fallback(2);
   if (!tc) {
     if (app.k != nullptr) {
       const int es = dtype == B2P_F32 ? 4 : 2;
-      if ((head_dim * es) % 4 != 0 || dtype < B2P_BF16 || dtype > B2P_F32) return B2P_EINVAL;
+      if ((head_dim * es) % 4 != 0) return B2P_EINVAL;
       const cudaStream_t st = static_cast<cudaStream_t>(stream);
       uint8_t* kp = static_cast<uint8_t*>(const_cast<void*>(key_cache));
       uint8_t* vp = static_cast<uint8_t*>(const_cast<void*>(value_cache));
@@ -940,21 +1023,17 @@ int decode_impl(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
                            num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, scale, out,
                            out_tok_stride, out_head_stride, dtype, err_flag, stream);
   }
-  if (!workspace) return B2P_EWORKSPACE;
-  int rc = prepare(pl);
-  if (rc != B2P_OK) return rc;
-  const int hpu = heads_per_unit(num_kv_heads, pl.warps);
-  const int64_t ctas = ctas_x(pl.ctas_per_sm, num_kv_heads, hpu);
-  const size_t need =
-      workspace_bytes(num_seqs, num_kv_heads, ctas * (pl.warps / hpu), pl.record);
-  if (workspace_size < need) return B2P_EWORKSPACE;
+  if (!workspace || workspace_size < rt.need) return B2P_EWORKSPACE;
+  const Plan& pl = rt.pl;
+  const int hpu = rt.hpu;
+  const int64_t ctas = rt.ctas;
 
   CUtensorMap kmap, vmap;
-  rc = b2p_host::pool_tensor_map(&kmap, key_cache, num_layers, num_slots, num_kv_heads,
-                                 head_dim, 2);
+  rc = b2p_host::pool_tensor_map_box(&kmap, key_cache, num_layers, num_slots, num_kv_heads,
+                                     head_dim, 2, 1);
   if (rc != B2P_OK) return rc;
-  rc = b2p_host::pool_tensor_map(&vmap, value_cache, num_layers, num_slots, num_kv_heads,
-                                 head_dim, 2);
+  rc = b2p_host::pool_tensor_map_box(&vmap, value_cache, num_layers, num_slots, num_kv_heads,
+                                     head_dim, 2, 1);
   if (rc != B2P_OK) return rc;
 
   DecodeParams p;
@@ -1090,21 +1169,27 @@ extern "C" int b2p_paged_decode_noalloc(const void* q, int64_t q_tok_stride,
                                         int block_size, float scale, void* out,
                                         int64_t out_tok_stride, int64_t out_head_stride,
                                         int dtype, int32_t* err_flag, void* stream) {
-  if (num_seqs < 0 || num_kv_heads <= 0) return B2P_EINVAL;
-  if (num_seqs == 0) return B2P_OK;
-  // The per-sequence counters alone must fit; the full requirement (which depends on the
-  // device's SM count) is checked against the array size by b2p_paged_decode below.
-  const size_t counters = counters_bytes(num_seqs, num_kv_heads);
-  if (counters > kNoAllocScratchBytes) return B2P_EWORKSPACE;
+  // Every argument and the workspace the chosen kernel needs are checked first, so a
+  // rejected call queues nothing on the stream.
+  DecodeRoute rt;
+  int rc = decode_route(q, q_tok_stride, q_head_stride, key_cache, value_cache, layer_index,
+                        num_layers, num_slots, block_tables, context_lens, num_seqs,
+                        num_q_heads, num_kv_heads, head_dim, block_size, out, dtype, rt,
+                        kNoAllocScratchBytes);
+  if (rc != B2P_OK || rt.empty) return rc;
   void* scratch = nullptr;
-  int rc = noalloc_scratch(&scratch);
-  if (rc != B2P_OK) return rc;
-  // The array keeps whatever the previous call left; the counters must start at zero.
-  cudaError_t e = cudaMemsetAsync(scratch, 0, counters, static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return b2p_host::record_error(e);
+  if (rt.tc) {  // the CUDA-core kernel uses no scratch
+    if (rt.need > kNoAllocScratchBytes) return B2P_EWORKSPACE;
+    rc = noalloc_scratch(&scratch);
+    if (rc != B2P_OK) return rc;
+    // The array keeps whatever the previous call left; the counters must start at zero.
+    const cudaError_t e = cudaMemsetAsync(scratch, 0, counters_bytes(num_seqs, num_kv_heads),
+                                          static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return b2p_host::record_error(e);
+  }
   return b2p_paged_decode(q, q_tok_stride, q_head_stride, key_cache, value_cache, layer_index,
                           num_layers, num_slots, block_tables, block_table_stride, context_lens,
                           num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, scale, out,
-                          out_tok_stride, out_head_stride, scratch, kNoAllocScratchBytes, dtype,
-                          err_flag, stream);
+                          out_tok_stride, out_head_stride, scratch,
+                          rt.tc ? kNoAllocScratchBytes : 0, dtype, err_flag, stream);
 }

@@ -1,7 +1,8 @@
 // K3 entry point: packed variable-length causal prefill / chunked prefill over the
-// paged pool. bf16/f16 with head_dim 128 and block sizes that are multiples of 16 run on
-// the tcgen05 kernel (prefill_tc.cu); other shapes run on the CUDA-core kernel in
-// attn_simt.cu.
+// paged pool. bf16/f16 with head_dim 64 or 128, block sizes that are multiples of 16 and
+// 16-byte aligned rows run on the tcgen05 kernel (prefill_tc.cu); fp32 and other shapes
+// run on the CUDA-core kernel in attn_simt.cu. A bf16/f16 call that takes the CUDA-core
+// kernel is counted (b2p_cuda_core_fallbacks(3)), since it runs many times slower.
 #include "common.cuh"
 
 int b2p_prefill_tc(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
@@ -44,6 +45,7 @@ extern "C" int b2p_paged_prefill(const void* q, int64_t q_tok_stride, int64_t q_
                                num_q_heads, num_kv_heads, head_dim, block_size, scale, out,
                                out_tok_stride, out_head_stride, dtype, err_flag, stream);
   if (rc != B2P_EUNSUPPORTED) return rc;
+  if (dtype != B2P_F32) b2p_host::note_fallback(3);
   return b2p_prefill_simt(q, q_tok_stride, q_head_stride, key_cache, value_cache, layer_index,
                           num_slots, block_tables, block_table_stride, cu_seqlens_q,
                           context_lens, num_seqs, total_q, num_q_heads, num_kv_heads, head_dim,

@@ -1106,15 +1106,41 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
 constexpr int kCounterSlots = 64;
 __device__ int32_t g_prefill_counters[kCounterSlots][2];
 
+// Device address of g_prefill_counters on the current device (looked up once per device).
+int prefill_counter_base(int32_t** out) {
+  static void* base[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return b2p_host::record_error(ce);
+  if (dev < 0 || dev >= 64) return B2P_EUNSUPPORTED;
+  std::lock_guard<std::mutex> lock(mu);
+  if (base[dev] == nullptr) {
+    ce = cudaGetSymbolAddress(&base[dev], g_prefill_counters);
+    if (ce != cudaSuccess) return b2p_host::record_error(ce);
+  }
+  *out = static_cast<int32_t*>(base[dev]);
+  return B2P_OK;
+}
+
 }  // namespace
+
+// Zero every prefill claim slot of the current device on `stream` (after a launch that
+// did not run to its end, e.g. one whose bounded waits gave up).
+int b2p_prefill_reset_counters(void* stream) {
+  int32_t* base = nullptr;
+  const int rc = prefill_counter_base(&base);
+  if (rc != B2P_OK) return rc;
+  const cudaError_t e = cudaMemsetAsync(base, 0, sizeof(int32_t) * 2 * kCounterSlots,
+                                        static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? B2P_OK : b2p_host::record_error(e);
+}
 
 // ====================================================================== host side
 namespace b2p_host {
 int tensor_map_4d_rows(CUtensorMap* out, const void* base, int64_t rows, int heads, int head_dim,
                        int64_t row_stride_elems, int64_t head_stride_elems, int elem_bytes,
                        int box_rows);
-int pool_tensor_map_box(CUtensorMap* out, const void* base, int64_t num_layers, int64_t num_slots,
-                        int num_kv_heads, int head_dim, int elem_bytes, int box_chunks);
 }  // namespace b2p_host
 
 // Launches the tcgen05 prefill when the shape allows it; returns B2P_EUNSUPPORTED otherwise
@@ -1162,24 +1188,12 @@ int b2p_prefill_tc(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
   p.err = err_flag;
   p.hq = num_q_heads;
   {
-    static void* base[64] = {nullptr};
-    static std::mutex mu;
     static std::atomic<uint32_t> next_slot{0};
-    int dev = 0;
-    cudaError_t ce = cudaGetDevice(&dev);
-    if (ce != cudaSuccess) return b2p_host::record_error(ce);
-    if (dev < 0 || dev >= 64) return B2P_EUNSUPPORTED;
-    void* addr = nullptr;
-    {
-      std::lock_guard<std::mutex> lock(mu);
-      if (base[dev] == nullptr) {
-        ce = cudaGetSymbolAddress(&base[dev], g_prefill_counters);
-        if (ce != cudaSuccess) return b2p_host::record_error(ce);
-      }
-      addr = base[dev];
-    }
+    int32_t* addr = nullptr;
+    const int crc = prefill_counter_base(&addr);
+    if (crc != B2P_OK) return crc;
     const uint32_t slot = next_slot.fetch_add(1) % kCounterSlots;
-    p.ctr = static_cast<int32_t*>(addr) + 2 * slot;
+    p.ctr = addr + 2 * slot;
   }
   const bool bf16 = dtype == B2P_BF16;
   const int variant = (bf16 ? 0 : 1) + (head_dim == 64 ? 2 : 0);

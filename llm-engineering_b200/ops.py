@@ -100,6 +100,21 @@ def kv_write(
     _lib.check(rc, "b2p_kv_write")
 
 
+def cuda_core_fallbacks() -> tuple[int, int]:
+    """bf16/f16 launches of (decode, prefill) so far that ran on the CUDA-core kernels
+    because the tensor-core kernels' preconditions were not met."""
+    lib = _lib.load()
+    return int(lib.b2p_cuda_core_fallbacks(2)), int(lib.b2p_cuda_core_fallbacks(3))
+
+
+def reset_scratch(device: torch.device) -> None:
+    """Zero the library's device-resident prefill claim counters on ``device`` (on its
+    current stream), after a launch whose bounded waits gave up."""
+    with torch.cuda.device(device):
+        _lib.check(_lib.load().b2p_reset_scratch(_stream(torch.device(device))),
+                   "b2p_reset_scratch")
+
+
 def decode_workspace_size(num_seqs: int, num_q_heads: int, num_kv_heads: int, head_dim: int) -> int:
     return int(_lib.load().b2p_paged_decode_workspace_size(num_seqs, num_q_heads, num_kv_heads,
                                                             head_dim))

@@ -34,6 +34,7 @@ from __future__ import annotations
 
 import contextlib
 import contextvars
+import warnings
 from collections.abc import Sequence
 from dataclasses import dataclass
 from typing import Any
@@ -43,6 +44,7 @@ import torch
 from transformers.cache_utils import Cache
 
 from . import ops as _ops
+from ._lib import DEV_WAIT_TIMEOUT
 
 ATTENTION_NAME = "b200_paged"
 PREFILL, DECODE = "prefill", "decode"
@@ -190,14 +192,19 @@ class B200PagedModelRunner:
         paged_cache: the reference's ``PagedKVCache`` (or anything with ``.storage``) or a
             storage object exposing ``key_cache``, ``value_cache`` and ``block_size``
             (the reference's ``PagedKVStorage`` or ``llm_engineering_b200.storage``).
-        kernels: the kernel module (tests substitute a CPU implementation).
+
+    Every ``forward`` reads the kernels' device error word once the step's logits are
+    computed (one synchronisation, which the caller's sampling would make anyway) and
+    raises ``RuntimeError`` if a kernel reported bad data (a slot or block id outside the
+    pool, a context length that does not fit, a bounded wait that gave up): the logits of
+    such a step are not returned.
     """
 
-    def __init__(self, model, device: torch.device, paged_cache, *, kernels: Any = None) -> None:
+    def __init__(self, model, device: torch.device, paged_cache) -> None:
         self._model = model
         self._device = torch.device(device)
         self._storage = _storage_of(paged_cache)
-        self._kernels = kernels if kernels is not None else _ops
+        self._warned_fallback = False
         _register_attention()
         model.set_attn_implementation(ATTENTION_NAME)
         model.eval()
@@ -212,6 +219,9 @@ class B200PagedModelRunner:
     @staticmethod
     def _token_ids(seq, start: int, stop: int) -> np.ndarray:
         """Token ids of positions [start, stop) without building the whole history."""
+        take = getattr(seq, "token_slice", None)
+        if take is not None:  # this package's sequences keep the history as one array
+            return take(start, stop)
         prompt = seq.request.prompt_token_ids
         n = len(prompt)
         if stop <= n:
@@ -288,20 +298,21 @@ class B200PagedModelRunner:
         rows = dev_i32[2 * n:3 * n]
         tables = dev_i32[3 * n:].view(n, width)
         total_q = int(sum(d["qlens"]))
-        md = self._kernels.build_metadata(qlens, ctx, rows, tables, d["block_size"], total_q, 0,
-                                          self._err)
-        need = self._kernels.decode_workspace_size(max(num_decode, 1), self._hq, self._hkv,
-                                                   self._head_dim)
+        kernels = _ops
+        md = kernels.build_metadata(qlens, ctx, rows, tables, d["block_size"], total_q, 0,
+                                    self._err)
+        need = kernels.decode_workspace_size(max(num_decode, 1), self._hq, self._hkv,
+                                             self._head_dim)
         if self._workspace.numel() < need:
             self._workspace = torch.zeros(need, dtype=torch.uint8, device=dev)
         batch = StepBatch(
-            kernels=self._kernels, key_cache=self._storage.key_cache,
+            kernels=kernels, key_cache=self._storage.key_cache,
             value_cache=self._storage.value_cache, block_size=d["block_size"], total_q=total_q,
             num_execs=n, num_decode=num_decode, max_q_len=max(d["qlens"]),
             slot_mapping=md["slot_mapping"], positions=md["positions"],
             cu_seqlens_q=md["cu_seqlens_q"], context_lens=ctx, block_tables=tables,
             logit_indices=md["logit_indices"], workspace=self._workspace, err=self._err,
-            fused_decode=num_decode > 0 and hasattr(self._kernels, "paged_decode_append"))
+            fused_decode=num_decode > 0 and hasattr(kernels, "paged_decode_append"))
         return batch, input_ids
 
     # ------------------------------------------------------------------ ModelRunner
@@ -309,6 +320,7 @@ class B200PagedModelRunner:
         """Next-token logits (B, vocab) for the executions, in their order."""
         if not executions:
             raise ValueError("At least one execution is required.")
+        fallbacks = self._fallbacks()
         batch, input_ids = self._build_batch(executions)
         cache = B200PagedCache(batch)
         token = _active_batch.set(batch)
@@ -320,13 +332,49 @@ class B200PagedModelRunner:
                                   logits_to_keep=batch.logit_indices)
         finally:
             _active_batch.reset(token)
+        bits = self.device_error()
+        if bits:
+            raise RuntimeError(
+                f"paged-attention kernels reported device error bits {bits:#x} "
+                f"({', '.join(_error_names(bits))}) in this step; its logits are discarded")
+        if fallbacks is not None and not self._warned_fallback and self._fallbacks() != fallbacks:
+            self._warned_fallback = True
+            warnings.warn(
+                f"{self._storage.key_cache.dtype} paged attention ran on the CUDA-core kernels "
+                "(block size, head_dim, GQA group or row alignment outside what the tensor-core "
+                "kernels take); expect a large slowdown", RuntimeWarning, stacklevel=2)
         return out.logits[0]
 
+    @staticmethod
+    def _fallbacks() -> tuple[int, int] | None:
+        """bf16/f16 launches that took the CUDA-core kernels so far (decode, prefill)."""
+        count = getattr(_ops, "cuda_core_fallbacks", None)
+        return None if count is None else count()
+
     def device_error(self) -> int:
-        """Bits the kernels reported since the last call (0 = none); clears them."""
+        """Bits the kernels reported since the last call (0 = none); clears them.
+
+        After a bounded wait gave up (``B2P_DEV_WAIT_TIMEOUT``) a launch may have left
+        split-K counters set: the decode workspace and the prefill claim counters are then
+        zeroed before the next step."""
         v = int(self._err.item())
-        self._err.zero_()
+        if v:
+            self._err.zero_()
+            if v & DEV_WAIT_TIMEOUT:
+                self._workspace.zero_()
+                reset = getattr(_ops, "reset_scratch", None)
+                if reset is not None:
+                    reset(self._device)
         return v
+
+
+_ERROR_BITS = ((1, "slot id outside the pool"), (2, "block id outside the pool"),
+               (4, "a bounded wait gave up"), (8, "a length that does not fit"))
+
+
+def _error_names(bits: int) -> list[str]:
+    return [name for bit, name in _ERROR_BITS if bits & bit] or ["unknown"]
+
 
 
 @contextlib.contextmanager

@@ -193,8 +193,8 @@ def _attend(qf: torch.Tensor, kf: torch.Tensor, vf: torch.Tensor, scale: float,
     s = torch.matmul(qh, kh.transpose(1, 2)) * scale
     if causal_offset is not None:
         tq, tk = s.shape[1], s.shape[2]
-        qpos = torch.arange(tq).unsqueeze(1) + causal_offset
-        kpos = torch.arange(tk).unsqueeze(0)
+        qpos = torch.arange(tq, device=s.device).unsqueeze(1) + causal_offset
+        kpos = torch.arange(tk, device=s.device).unsqueeze(0)
         s = s.masked_fill(kpos > qpos, float("-inf"))
     p = torch.softmax(s, dim=-1, dtype=torch.float32)
     return torch.matmul(p, vh).transpose(0, 1)

@@ -554,3 +554,121 @@ def test_prefill_trailing_slice_of_packed_batch(ops):
     expect = ref.prefill_attention(q, kc, vc, 0, tables[2:], cu[2:], ctx[2:], bs, d ** -0.5)
     close(out[2:], expect, torch.bfloat16)
     assert torch.count_nonzero(out[:2].float()) == 0  # decode rows untouched
+
+
+# ------------------------------------------------------------------ parity at benchmark sizes
+def test_decode_large_values_in_split_sequences(ops):
+    """V rows of magnitude ~1e5 (representable in bf16, far past fp16's 65,504) in
+    sequences cut across many stream units, so their partial records go through the merge.
+    Attention is linear in V, so the output divided by the V scale must meet the usual bf16
+    bounds against the fp32 oracle, and every value must be finite."""
+    dev = torch.device("cuda")
+    hq, hkv, d, bs = 12, 2, 128, 16
+    scale_v = 1.0e5
+    rng = np.random.default_rng(130)
+    ctx = [120_000, 9_000] + rng.integers(2_000, 6_000, size=40).tolist()
+    nb = sum((c + bs - 1) // bs for c in ctx) + 3
+    kc, vc = make_pool(131, 1, nb, bs, hkv, d, torch.float32)
+    vc = (vc * scale_v).to(torch.bfloat16)
+    kc = kc.to(torch.bfloat16)
+    tables, bt = make_tables(132, ctx, bs, nb)
+    q = torch.randn(len(ctx), hq, d, generator=torch.Generator().manual_seed(133)).to(torch.bfloat16)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = ops.paged_decode(q.to(dev), kc.to(dev), vc.to(dev), 0, bt.to(dev),
+                           torch.tensor(ctx, dtype=torch.int32, device=dev), bs, d ** -0.5,
+                           err_flag=err)
+    assert int(err.item()) == 0
+    assert torch.isfinite(out.float()).all()
+    expect = ref.decode_attention(q, kc, vc, 0, tables, ctx, bs, d ** -0.5)
+    assert expect.abs().max().item() > 65504.0  # the range fp16 records could not hold
+    close(out.float() / scale_v, expect / scale_v, torch.bfloat16)
+
+
+def test_decode_7b_long_context_churn_full_size(ops):
+    """The long-context configuration at its full per-GPU size: Qwen2.5-7B attention shape
+    (28 Q / 4 KV heads, head_dim 128), 64 sequences with contexts U[8192, 32768], block
+    size 16, tables fragmented by 30% alloc/free churn; the fused write + decode call the
+    benchmark runs, against the oracle's scatter + decode."""
+    import bench
+
+    dev = torch.device("cuda")
+    w = bench.make_longctx_workload(2024, dev, layers=1)
+    hq, hkv, d, bs = bench.LC_HQ, bench.LC_HKV, bench.HEAD_DIM, bench.BLOCK_SIZE
+    kd, vd = w["kc"], w["vc"]
+    tables = w["table_lists"]
+    ctx = w["ctx"].tolist()
+    kc, vc = kd.cpu(), vd.cpu()  # the pool before the fused call stores the new rows
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = ops.paged_decode_append(w["q"][0], w["new_k"][0], w["new_v"][0], kd, vd, 0,
+                                  torch.from_numpy(w["tables"]).to(dev),
+                                  torch.from_numpy(w["ctx"]).to(dev), bs, d ** -0.5,
+                                  err_flag=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    slots = [t[(c - 1) // bs] * bs + (c - 1) % bs for t, c in zip(tables, ctx)]
+    ref.scatter(kc, vc, 0, slots, w["new_k"][0].cpu(), w["new_v"][0].cpu())
+    rows = torch.tensor(slots, dtype=torch.long)
+    assert torch.equal(kd[0, rows.to(dev)].cpu(), kc[0, rows])
+    assert torch.equal(vd[0, rows.to(dev)].cpu(), vc[0, rows])
+    expect = ref.decode_attention(w["q"][0].cpu(), kc, vc, 0, tables, ctx, bs, d ** -0.5)
+    close(out, expect, torch.bfloat16)
+    assert (hq, hkv) == (28, 4) and len(ctx) == 64 and min(ctx) >= 8192 and max(ctx) <= 32768
+
+
+def test_prefill_full_benchmark_workload_and_chunks(ops):
+    """The prefill benchmark's workload at full size (32 prompts log-uniform in [64, 8192],
+    49,659 packed tokens, fragmented pool, bf16, 12/2 heads, head_dim 128): K1 writes every
+    prompt token, K3 runs the packed causal attention, and the result is compared with the
+    oracle's scatter + per-prompt causal attention. Then the prompts longer than 2,048
+    tokens are run again as chunked-prefill slices (a middle slice and the last 512 rows of
+    each, packed into one launch, attending to the history already in the pool), whose rows
+    must match the same rows of the whole-prompt oracle."""
+    import bench
+
+    dev = torch.device("cuda")
+    w = bench.make_prefill_workload(4321, dev)
+    bs, d = bench.BLOCK_SIZE, bench.HEAD_DIM
+    lens = w["lens"].astype(np.int64)
+    cu = w["cu"].tolist()
+    ctx = lens.astype(np.int32)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    slots = torch.from_numpy(w["slots"]).to(dev)
+    ops.kv_write(w["kc"], w["vc"], 0, slots, w["k"], w["v"], err)
+    bt = torch.from_numpy(w["tables"]).to(dev)
+    out = ops.paged_prefill(w["q"], w["kc"], w["vc"], 0, bt,
+                            torch.from_numpy(w["cu"]).to(dev), torch.from_numpy(ctx).to(dev),
+                            int(lens.max()), bs, d ** -0.5, err_flag=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert int(lens.sum()) == 49_659 and int(lens.max()) == 6_818
+
+    tables = [row[row >= 0].tolist() for row in w["tables"]]
+    kc = torch.zeros(w["kc"].shape, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    q_cpu = w["q"].cpu()
+    ref.scatter(kc, vc, 0, w["slots"].tolist(), w["k"].cpu(), w["v"].cpu())
+    assert torch.equal(w["kc"].cpu(), kc) and torch.equal(w["vc"].cpu(), vc)
+    expect = ref.prefill_attention(q_cpu, kc, vc, 0, tables, cu, lens.tolist(), bs, d ** -0.5)
+    close(out, expect, torch.bfloat16)
+
+    # chunked-prefill slices of the long prompts, packed into one launch
+    rows, c_tables, c_ctx, c_cu = [], [], [], [0]
+    for i, n in enumerate(lens.tolist()):
+        if n <= 2048:
+            continue
+        for a, b in ((n // 2 - 300, n // 2 + 100), (n - 512, n)):
+            rows.append(np.arange(cu[i] + a, cu[i] + b))
+            c_tables.append(w["tables"][i])
+            c_ctx.append(b)
+            c_cu.append(c_cu[-1] + (b - a))
+    rows = np.concatenate(rows)
+    assert len(c_ctx) >= 8
+    q_chunks = w["q"][torch.from_numpy(rows).to(dev)]
+    out_c = ops.paged_prefill(q_chunks, w["kc"], w["vc"], 0,
+                              torch.from_numpy(np.stack(c_tables)).to(dev),
+                              torch.tensor(c_cu, dtype=torch.int32, device=dev),
+                              torch.tensor(c_ctx, dtype=torch.int32, device=dev), 512, bs,
+                              d ** -0.5, err_flag=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    close(out_c, expect[torch.from_numpy(rows)], torch.bfloat16)

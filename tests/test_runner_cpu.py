@@ -1,7 +1,8 @@
 """Host logic of B200PagedModelRunner on CPU, against the reference-style packed runner.
 
-The runner's kernel module is replaced by a CPU stand-in built from the oracle (this file
-only): the test checks the runner's own work — per-step metadata, the HF cache hook, the
+The runner's kernel module is monkeypatched, in this file only, with a CPU stand-in built
+from the oracle (the product has no such seam: its runner always calls the CUDA ops): the
+test checks the runner's own work — per-step metadata, the HF cache hook, the
 registered attention function, the decode/prefill split and the logit rows — on a tiny
 random Qwen2, driving both runners with this package's engine. The CUDA kernels
 themselves are checked on the GPU (test_kernels_gpu.py, test_runner_gpu.py).
@@ -16,6 +17,7 @@ import pytest
 import torch
 
 from llm_engineering_b200 import engine as eng
+from llm_engineering_b200 import runner as runner_mod
 from llm_engineering_b200.runner import B200PagedModelRunner
 from oracle import paged as ref
 from oracle.runner import ReferencePackedRunner
@@ -90,6 +92,11 @@ class CpuKernels:
         }
 
 
+@pytest.fixture(autouse=True)
+def cpu_kernels(monkeypatch):
+    monkeypatch.setattr(runner_mod, "_ops", CpuKernels())
+
+
 def tiny_model(seed=0):
     from transformers import Qwen2Config, Qwen2ForCausalLM
 
@@ -124,7 +131,7 @@ def test_runner_matches_reference_packed_path(block_size, num_blocks):
                                   max_batched_tokens=40)
     kc, vc = pool(2, num_blocks, block_size, 2, 16)
     ours = B200PagedModelRunner(copy.deepcopy(model), torch.device("cpu"),
-                                _Storage(kc, vc, block_size), kernels=CpuKernels())
+                                _Storage(kc, vc, block_size))
     kr, vr = pool(2, num_blocks, block_size, 2, 16)
     theirs = ReferencePackedRunner(copy.deepcopy(model), kr, vr, block_size)
     got = run_engine(ours, requests, cfg)
@@ -139,8 +146,7 @@ def test_runner_logits_match_for_mixed_step_and_reference_style_slots():
     bs = 4
     kc, vc = pool(2, 32, bs, 2, 16)
     kr, vr = pool(2, 32, bs, 2, 16)
-    ours = B200PagedModelRunner(copy.deepcopy(model), torch.device("cpu"), _Storage(kc, vc, bs),
-                                kernels=CpuKernels())
+    ours = B200PagedModelRunner(copy.deepcopy(model), torch.device("cpu"), _Storage(kc, vc, bs))
     theirs = ReferencePackedRunner(copy.deepcopy(model), kr, vr, bs)
 
     def execs(phase_a):
@@ -180,21 +186,19 @@ def test_chunked_prefill_runs_give_the_tokens_of_whole_prefill():
     whole_cfg = eng.EngineConfiguration(block_size=bs, num_blocks=nb, max_sequences=4,
                                         max_batched_tokens=128)
     kc, vc = pool(2, nb, bs, 2, 16)
-    whole = B200PagedModelRunner(copy.deepcopy(model), torch.device("cpu"), _Storage(kc, vc, bs),
-                                 kernels=CpuKernels())
+    whole = B200PagedModelRunner(copy.deepcopy(model), torch.device("cpu"), _Storage(kc, vc, bs))
     expect = run_engine(whole, requests, whole_cfg)
     chunk_cfg = eng.EngineConfiguration(block_size=bs, num_blocks=nb, max_sequences=4,
                                         max_batched_tokens=12, enable_chunked_prefill=True)
     kc2, vc2 = pool(2, nb, bs, 2, 16)
     chunked = B200PagedModelRunner(copy.deepcopy(model), torch.device("cpu"),
-                                   _Storage(kc2, vc2, bs), kernels=CpuKernels())
+                                   _Storage(kc2, vc2, bs))
     assert run_engine(chunked, requests, chunk_cfg) == expect
 
 
 def test_runner_rejects_empty_batch():
     kc, vc = pool(2, 8, 4, 2, 16)
-    ours = B200PagedModelRunner(tiny_model(), torch.device("cpu"), _Storage(kc, vc, 4),
-                                kernels=CpuKernels())
+    ours = B200PagedModelRunner(tiny_model(), torch.device("cpu"), _Storage(kc, vc, 4))
     with pytest.raises(ValueError, match="At least one execution is required."):
         ours.forward([])
 

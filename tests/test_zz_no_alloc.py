@@ -5,8 +5,9 @@ b2p_paged_decode_noalloc exists for callers that cannot give the library device 
 language with no device allocator). It keeps the split-K scratch in an array compiled
 into the library instead. These tests call it through the C ABI and check that two calls
 in a row give the results of b2p_paged_decode with a caller-allocated workspace, within
-the bf16 tolerance used by the other decode tests, and that an oversized problem is
-refused before anything runs. The file is named to be collected last.
+the bf16 tolerance used by the other decode tests, and those of the fp32 oracle, and that
+a problem too large for the array is refused before anything is queued. The file is named
+to be collected last.
 """
 
 from __future__ import annotations
@@ -18,6 +19,7 @@ import pytest
 import torch
 
 from llm_engineering_b200 import _lib
+from oracle import paged as ref
 
 
 def _call_noalloc(q, kc, vc, bt, ctx, out, bs, scale, err):
@@ -56,6 +58,8 @@ def test_noalloc_decode_matches_workspace_decode_twice(ops):
     scale = d ** -0.5
 
     expect = ops.paged_decode(q, kc, vc, 0, bt, ctx_d, bs, scale)
+    tables = [row[row >= 0].tolist() for row in bt.cpu().numpy()]
+    oracle = ref.decode_attention(q.cpu(), kc.cpu(), vc.cpu(), 0, tables, ctx, bs, scale)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     for _ in range(2):  # the second call reuses the scratch the first one left behind
         out = torch.full_like(q, float("nan"))
@@ -63,8 +67,30 @@ def test_noalloc_decode_matches_workspace_decode_twice(ops):
         assert rc == _lib.B2P_OK, _lib.status_text(rc)
         torch.cuda.synchronize()
         assert int(err.item()) == 0
-        diff = (out.float() - expect.float()).abs()
-        assert diff.max().item() < 2e-2 and diff.mean().item() < 2e-3
+        for want in (expect.float(), oracle.to(dev)):
+            diff = (out.float() - want).abs()
+            assert diff.max().item() < 2e-2 and diff.mean().item() < 2e-3
+
+
+@pytest.mark.gpu
+def test_noalloc_decode_refuses_when_only_the_counters_fit(ops):
+    """Counters that fit the array but split-K records that do not: the call is refused
+    with a workspace error and leaves the output untouched (nothing was queued)."""
+    dev = torch.device("cuda")
+    hq, hkv, d, bs = 12, 2, 128, 16
+    n = 250_000  # 2 MB of counters; with the records (~15 MB on 148 SMs) past 16 MiB
+    need = ops.decode_workspace_size(n, hq, hkv, d)
+    assert need > (16 << 20) and hkv * n * 4 < (16 << 20)
+    kc = torch.zeros(1, 4 * bs, hkv, d, dtype=torch.bfloat16, device=dev)
+    bt = torch.zeros(n, 1, dtype=torch.int32, device=dev)
+    ctx_d = torch.ones(n, dtype=torch.int32, device=dev)
+    q = torch.zeros(n, hq, d, dtype=torch.bfloat16, device=dev)
+    out = torch.full_like(q, 7.0)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    rc = _call_noalloc(q, kc, kc, bt, ctx_d, out, bs, d ** -0.5, err)
+    torch.cuda.synchronize()
+    assert rc == _lib.B2P_EWORKSPACE
+    assert bool((out == 7.0).all()) and int(err.item()) == 0
 
 
 def test_noalloc_decode_refuses_oversized_problem_without_a_gpu_call():
