@@ -13,7 +13,10 @@ class EngineConfiguration:
     ``EngineConfiguration`` (serving/engine/config.py:6-60), so configurations move
     between the two engines unchanged, plus ``enable_chunked_prefill`` (off by default,
     which keeps the reference's policy): prompts longer than ``max_batched_tokens`` are
-    then admitted and prefilled over several steps in chunks that fit the step's budget.
+    then admitted and prefilled over several steps in chunks that fit the step's budget;
+    ``max_prefill_chunk`` (chunked prefill only; None = no limit) caps the tokens one
+    prefill contributes to a step, so that a step's prefill budget is shared by several
+    prompts (e.g. 4 slices of 512 tokens).
     """
 
     device: str = "cpu"
@@ -24,6 +27,7 @@ class EngineConfiguration:
     max_batched_tokens: int = 2_048
     seed: int = 0
     enable_chunked_prefill: bool = False
+    max_prefill_chunk: int | None = None
 
     def __post_init__(self) -> None:
         if not self.device.strip():
@@ -47,3 +51,8 @@ class EngineConfiguration:
             )
         if self.seed < 0:
             raise ValueError("seed must not be negative.")
+        if self.max_prefill_chunk is not None:
+            if self.max_prefill_chunk <= 0:
+                raise ValueError("max_prefill_chunk must be greater than zero.")
+            if not self.enable_chunked_prefill:
+                raise ValueError("max_prefill_chunk requires enable_chunked_prefill.")

@@ -9,9 +9,10 @@ admitted other running sequence is preempted (blocks freed, put back at the head
 waiting queue) and re-prefilled later.
 
 With ``enable_chunked_prefill`` (not in the reference, off by default) a prefill may be
-cut to the step's remaining budget: after the decodes, sequences whose prefill is under
-way continue first (in admission order), then waiting sequences are admitted as before,
-the last one taking whatever budget is left. A sequence decodes once all of its history
+cut to the step's remaining budget (and to ``max_prefill_chunk`` tokens when set): after
+the decodes, sequences whose prefill is under way continue first (in admission order),
+then waiting sequences are admitted as before, the last one taking whatever budget is
+left. A sequence decodes once all of its history
 is in the pool; preemption drops the progress and the sequence is re-prefilled later.
 """
 
@@ -149,6 +150,7 @@ class Scheduler:
 
     def _schedule_chunked(self) -> SchedulerOutput:
         budget = self.configuration.max_batched_tokens
+        cap = self.configuration.max_prefill_chunk or budget
         decode = tuple(s for s in self._running if s.request.request_id not in self._prefilled)
         budget -= len(decode)
         prefill: list[SequenceState] = []
@@ -159,7 +161,7 @@ class Scheduler:
             done = self._prefilled.get(seq.request.request_id)
             if done is None:
                 continue
-            n = min(seq.current_length - done, budget)
+            n = min(seq.current_length - done, budget, cap)
             prefill.append(seq)
             chunks.append((done, n))
             budget -= n
@@ -169,7 +171,7 @@ class Scheduler:
                 break
             self._admit(head)
             self._prefilled[head.request.request_id] = 0
-            n = min(head.current_length, budget)
+            n = min(head.current_length, budget, cap)
             prefill.append(head)
             chunks.append((0, n))
             budget -= n

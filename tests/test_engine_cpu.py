@@ -156,6 +156,36 @@ def test_chunked_prefill_admits_long_prompts_and_splits_them_to_the_budget():
         s.complete_prefill_chunk(out.prefill_sequences[1], 6)
 
 
+def test_prefill_chunk_cap_shares_the_budget_between_prompts():
+    """max_prefill_chunk = 4 with a 14-token budget and one decode: three prompts each get a
+    4-token slice in one step (13 tokens), and the slices continue in admission order."""
+    cfg = eng.EngineConfiguration(block_size=4, num_blocks=64, max_sequences=8,
+                                  max_batched_tokens=14, enable_chunked_prefill=True,
+                                  max_prefill_chunk=4)
+    s = eng.Scheduler(cfg)
+    s.submit(eng.Request("d", (1, 2), 4))
+    out = s.schedule()
+    assert out.prefill_chunks == ((0, 2),)
+    assert s.complete_prefill_chunk(out.prefill_sequences[0], 2) is True
+    s.reserve_generated_token(out.prefill_sequences[0])
+    out.prefill_sequences[0].append_token(9)
+    for rid, n in (("a", 10), ("b", 6), ("c", 9), ("e", 3)):
+        s.submit(eng.Request(rid, tuple(range(n)), 2))
+    out = s.schedule()
+    assert [q.request.request_id for q in out.decode_sequences] == ["d"]
+    assert [q.request.request_id for q in out.prefill_sequences] == ["a", "b", "c", "e"]
+    assert out.prefill_chunks == ((0, 4), (0, 4), (0, 4), (0, 1))
+    assert out.num_batched_tokens == 14
+    for q, (_, n) in zip(out.prefill_sequences, out.prefill_chunks):
+        s.complete_prefill_chunk(q, n)
+    out = s.schedule()
+    assert out.prefill_chunks == ((4, 4), (4, 2), (4, 4), (1, 2))
+    with pytest.raises(ValueError, match="requires enable_chunked_prefill"):
+        eng.EngineConfiguration(max_prefill_chunk=4)
+    with pytest.raises(ValueError, match="max_prefill_chunk must be greater than zero"):
+        eng.EngineConfiguration(enable_chunked_prefill=True, max_prefill_chunk=0)
+
+
 def test_chunked_prefill_gives_the_tokens_of_whole_prefill():
     """The stand-in model's token depends on (request, history length) only, so every
     request must finish with the same tokens whether its prompt was prefilled whole or in

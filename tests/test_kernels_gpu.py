@@ -558,18 +558,18 @@ def test_prefill_trailing_slice_of_packed_batch(ops):
 
 # ------------------------------------------------------------------ parity at benchmark sizes
 def test_decode_large_values_in_split_sequences(ops):
-    """V rows of magnitude ~1e5 (representable in bf16, far past fp16's 65,504) in
-    sequences cut across many stream units, so their partial records go through the merge.
-    Attention is linear in V, so the output divided by the V scale must meet the usual bf16
-    bounds against the fp32 oracle, and every value must be finite."""
+    """V rows around 4e5 (N(0,1) x 1e5 + 4e5: representable in bf16, far past fp16's
+    65,504) in sequences cut across many stream units, so that every partial record the
+    merge reads holds values beyond fp16's range. Outputs must be finite and within a
+    bf16-sized relative error of the fp32 oracle: at most 1e-2 for any element and 3e-3
+    on average (one bf16 rounding of the output is up to 2.6e-3 relative here)."""
     dev = torch.device("cuda")
     hq, hkv, d, bs = 12, 2, 128, 16
-    scale_v = 1.0e5
     rng = np.random.default_rng(130)
     ctx = [120_000, 9_000] + rng.integers(2_000, 6_000, size=40).tolist()
     nb = sum((c + bs - 1) // bs for c in ctx) + 3
     kc, vc = make_pool(131, 1, nb, bs, hkv, d, torch.float32)
-    vc = (vc * scale_v).to(torch.bfloat16)
+    vc = (vc * 1.0e5 + 4.0e5).to(torch.bfloat16)
     kc = kc.to(torch.bfloat16)
     tables, bt = make_tables(132, ctx, bs, nb)
     q = torch.randn(len(ctx), hq, d, generator=torch.Generator().manual_seed(133)).to(torch.bfloat16)
@@ -580,8 +580,10 @@ def test_decode_large_values_in_split_sequences(ops):
     assert int(err.item()) == 0
     assert torch.isfinite(out.float()).all()
     expect = ref.decode_attention(q, kc, vc, 0, tables, ctx, bs, d ** -0.5)
-    assert expect.abs().max().item() > 65504.0  # the range fp16 records could not hold
-    close(out.float() / scale_v, expect / scale_v, torch.bfloat16)
+    assert expect.abs().min().item() > 65504.0  # beyond what fp16 records could hold
+    rel = (out.float().cpu() - expect).abs() / expect.abs()
+    assert rel.max().item() < 1e-2, rel.max().item()
+    assert rel.mean().item() < 3e-3, rel.mean().item()
 
 
 def test_decode_7b_long_context_churn_full_size(ops):
