@@ -18,8 +18,11 @@ and attends over the paged history. Each launch reads ~0.6 GB of K/V, more than 
               streams, layer by layer, so the copies overlap the other layers' attention).
 ``roofline``  HBM bytes the decode kernel must move per launch (1,024 B x sum(ctx) of K+V,
               plus Q/O, the new K/V rows read and stored, and block tables) / its mean
-              launch time (CUDA events around every launch of the timed region), against
-              the measured copy bandwidth in MEASURED_PEAKS.json.
+              launch time, against the measured copy bandwidth in MEASURED_PEAKS.json. The
+              timed region holds nothing but K2 launches, so the mean launch time is the
+              region's CUDA-event length / launches (gaps between launches included);
+              ``kernel_us_events`` gives the kernels' own durations from a second pass of
+              the same steps with events around every launch.
 ``clocks``    SM clock and throttle reasons sampled through NVML every 10 ms during the
               timed region; ``sustained`` repeats the step for >= 2 s with its own clocks.
 
@@ -371,27 +374,34 @@ def decode_timing(run: Run, ops, w: dict, hq: int, hkv: int, steps: int, warmup:
     for _ in range(warmup):
         step()
     run.barrier()
-    k_ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-             for _ in range(layers)] for _ in range(steps)]
+    # The timed region holds the K2 launches alone (events only at its two ends): its
+    # length / launches is each launch's average duration, inter-launch gaps included.
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev) as clocks:
         t0.record(stream)
-        for i in range(steps):
-            step(k_ev[i])
+        for _ in range(steps):
+            step()
         t1.record(stream)
         torch.cuda.synchronize(dev)
     run.barrier()
     ms = t0.elapsed_time(t1)
+    # The same steps again with events around every launch: the kernels' own durations.
+    k_ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+             for _ in range(layers)] for _ in range(steps)]
+    for i in range(steps):
+        step(k_ev[i])
+    torch.cuda.synchronize(dev)
     k2_ms = statistics.mean(a.elapsed_time(b) for st in k_ev for a, b in st)
     if int(err.item()) != 0:
         raise RuntimeError(f"device error flag set: {int(err.item())}")
     ms, k2_ms = run.max(ms, k2_ms)
-    res = {"ms": ms, "k2_ms": k2_ms, "clocks": clocks.summary(), "launches": layers * steps}
+    res = {"ms": ms, "k2_ms": k2_ms, "launch_ms": ms / (layers * steps),
+           "clocks": clocks.summary(), "launches": layers * steps}
 
     if sustain_s > 0:
         # >= sustain_s seconds of the same step (the same count on every rank), so that the
         # clock record covers a long stretch of the kernel under load
-        n_sus = max(steps, int(math.ceil(sustain_s / (ms / steps / 1e3))))
+        n_sus = max(steps, int(math.ceil(1.1 * sustain_s / (ms / steps / 1e3))))
         s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(dev) as sus_clocks:
             s0.record(stream)
@@ -478,7 +488,7 @@ def decode_line(run: Run, ops, args) -> dict:
                       sustain_s=0.0 if args.quick else SUSTAIN_S)
     peaks = _peaks()
     alg = algorithmic_bytes(w["ctx"])
-    achieved = alg / (r["k2_ms"] / 1e3) / 1e9
+    achieved = alg / (r["launch_ms"] / 1e3) / 1e9
     line = {
         "metric": METRIC,
         "value": round(NUM_SEQS * args.steps * run.world / (r["ms"] / 1e3), 1),
@@ -505,7 +515,10 @@ def decode_line(run: Run, ops, args) -> dict:
             "peak_source": f"{peaks['source']} hbm_gbs",
             "frac_of_8000": round(achieved / 8000.0, 4),
             "traffic": K2_TRAFFIC_BYTES, "algorithmic_bytes": alg,
-            "kernel": "paged_decode_tc (fused KV write)", "kernel_us": round(r["k2_ms"] * 1e3, 2),
+            "kernel": "paged_decode_tc (fused KV write)",
+            "kernel_us": round(r["launch_ms"] * 1e3, 2),
+            "kernel_us_timing": "timed region / launches (K2 is every launch of the step)",
+            "kernel_us_events": round(r["k2_ms"] * 1e3, 2),
         },
         "e2e": {
             "value": round(NUM_SEQS * args.steps * run.world / (r["e2e_ms"] / 1e3), 1),
@@ -527,7 +540,7 @@ def longctx_section(run: Run, ops, args, layers: int = NUM_LAYERS) -> dict:
     r = decode_timing(run, ops, w, LC_HQ, LC_HKV, args.steps, args.warmup, e2e=not args.quick)
     peaks = _peaks()
     alg = algorithmic_bytes(w["ctx"], LC_HQ, LC_HKV)
-    achieved = alg / (r["k2_ms"] / 1e3) / 1e9
+    achieved = alg / (r["launch_ms"] / 1e3) / 1e9
     sec = {
         "metric": "decode tok/s (long context, Qwen2.5-7B attention shape, 28 layers)",
         "value": round(LC_SEQS * args.steps * run.world / (r["ms"] / 1e3), 1),
@@ -544,7 +557,9 @@ def longctx_section(run: Run, ops, args, layers: int = NUM_LAYERS) -> dict:
                      "frac_of_8000": round(achieved / 8000.0, 4),
                      "traffic": LC_K2_TRAFFIC_BYTES, "algorithmic_bytes": alg,
                      "kernel": "paged_decode_tc (fused KV write)",
-                     "kernel_us": round(r["k2_ms"] * 1e3, 2)},
+                     "kernel_us": round(r["launch_ms"] * 1e3, 2),
+                     "kernel_us_timing": "timed region / launches",
+                     "kernel_us_events": round(r["k2_ms"] * 1e3, 2)},
         "gpu_launches": r["launches"],
         "clocks": r["clocks"],
     }
@@ -762,21 +777,37 @@ def qwen2_1p5b(dev: torch.device):
 
 
 class RequestStream:
-    """Seeded synthetic requests: prompt ids uniform over the vocabulary, prompt lengths
-    uniform in [128, 2048], 256 output tokens, greedy, EOS ignored."""
+    """This rank's share of one seeded synthetic request stream: prompt ids uniform over
+    the vocabulary, prompt lengths uniform in [128, 2048], 256 output tokens (or a budget
+    drawn uniformly in [1, 256] when ``staggered``), greedy, EOS ignored.
 
-    def __init__(self, seed: int) -> None:
+    Every rank draws the same stream and keeps the requests that the replica router
+    (``ReplicaRouter``, round robin by arrival index) assigns to it, so the ranks shard the
+    stream as independent engine replicas without exchanging a message."""
+
+    def __init__(self, seed: int, rank: int = 0, world: int = 1) -> None:
+        from llm_engineering_b200.replicas import ReplicaRouter
+
         self.rng = np.random.default_rng(seed)
+        self.router = ReplicaRouter(world, "round_robin", BLOCK_SIZE)
+        self.rank = rank
         self.count = 0
 
-    def next(self, max_new_tokens: int = MIX_OUT):
+    def _draw(self, staggered: bool):
         from llm_engineering_b200 import engine as eng
 
         n = int(self.rng.integers(MIX_PROMPT_LO, MIX_PROMPT_HI + 1))
         ids = tuple(self.rng.integers(0, MODEL_SHAPE["vocab_size"], size=n).tolist())
+        budget = int(self.rng.integers(1, MIX_OUT + 1)) if staggered else MIX_OUT
         self.count += 1
         return eng.Request(request_id=f"q{self.count}", prompt_token_ids=ids,
-                           max_new_tokens=max_new_tokens, ignore_eos=True)
+                           max_new_tokens=budget, ignore_eos=True)
+
+    def next(self, staggered: bool = False):
+        while True:
+            request = self._draw(staggered)
+            if self.router.assign(request) == self.rank:
+                return request
 
 
 def mixed_engine(dev: torch.device, model):
@@ -885,16 +916,18 @@ def model_section(run: Run, args) -> dict:
     dev, stream = run.dev, run.stream
     model = qwen2_1p5b(dev)
     engine, runner = mixed_engine(dev, model)
-    reqs = RequestStream(7 + run.rank)
+    reqs = RequestStream(7, run.rank, run.world)
     # the first population with staggered output budgets, so completions (and the
     # admissions that replace them) are spread over the run instead of arriving together
     for _ in range(MIX_DECODES + MIX_SLICES):
-        engine.submit(reqs.next(int(reqs.rng.integers(1, MIX_OUT + 1))))
-    for _ in range(max(args.warmup, MIX_WARMUP_STEPS)):
+        engine.submit(reqs.next(staggered=True))
+    warmup = args.mix_warmup if args.mix_warmup is not None else max(args.warmup,
+                                                                     MIX_WARMUP_STEPS)
+    for _ in range(warmup):
         _top_up(engine, reqs)
         engine.step()
     run.barrier()
-    steps = max(args.steps, MIX_TIMED_STEPS)
+    steps = args.mix_steps if args.mix_steps is not None else max(args.steps, MIX_TIMED_STEPS)
     fallbacks = ops.cuda_core_fallbacks()
     comp = {"decode_rows": 0, "prefill_tokens": 0, "steps": 0, "steps_with_decode": 0,
             "steps_with_prefill": 0}
@@ -946,7 +979,7 @@ def model_section(run: Run, args) -> dict:
         "metric": "output tok/s (engine + B200PagedModelRunner, random-init Qwen2.5-1.5B, "
                   "saturated closed loop)",
         "value": round(tokens * run.world / (dev_ms / 1e3), 1),
-        "unit": "tok/s", "steps": steps, "warmup": max(args.warmup, MIX_WARMUP_STEPS),
+        "unit": "tok/s", "steps": steps, "warmup": warmup,
         "ms_per_step": round(dev_ms / steps, 3),
         "dtype": "bf16",
         "data": "synthetic (seeded prompt ids, prompts U[128,2048], 256 output tokens)",
@@ -980,12 +1013,15 @@ def model_section(run: Run, args) -> dict:
 
 
 def offered_load(run: Run, engine, reqs: RequestStream, duration_s: float) -> dict:
-    """Poisson arrivals at MIX_RATE requests/s (exponential gaps from a seeded generator, as
-    serving/benchmark/workload.py:122-168 draws them) into a fresh engine for duration_s
-    seconds of wall time: output tokens/s, time to first token and time per output token."""
-    gaps = random.Random(11 + run.rank)
+    """Poisson arrivals (exponential gaps from a seeded generator, as
+    serving/benchmark/workload.py:122-168 draws them) at MIX_RATE x N requests/s into the
+    whole job, routed round robin, i.e. MIX_RATE requests/s into each rank's fresh engine,
+    for duration_s seconds of wall time: output tokens/s, time to first token and time per
+    output token."""
+    gaps = random.Random(11)
+    rate = MIX_RATE * run.world
     start = time.perf_counter()
-    next_at = start + gaps.expovariate(MIX_RATE)
+    next_at = start + gaps.expovariate(rate)
     arrived, first, done = {}, {}, {}
     tokens_before = _generated(engine)
     while True:
@@ -993,10 +1029,11 @@ def offered_load(run: Run, engine, reqs: RequestStream, duration_s: float) -> di
         if now - start >= duration_s:
             break
         while next_at <= now:
-            r = reqs.next()
-            engine.submit(r)
-            arrived[r.request_id] = next_at
-            next_at += gaps.expovariate(MIX_RATE)
+            r = reqs._draw(False)
+            if reqs.router.assign(r) == reqs.rank:
+                engine.submit(r)
+                arrived[r.request_id] = next_at
+            next_at += gaps.expovariate(rate)
         if not engine.has_unfinished_requests:
             time.sleep(max(0.0, min(next_at - now, 0.005)))
             continue
@@ -1028,6 +1065,99 @@ def offered_load(run: Run, engine, reqs: RequestStream, duration_s: float) -> di
         "tpot_ms_mean": round(1e3 * statistics.mean(tpot), 2) if tpot else None,
         "note": "wall-clock rates on each rank's host; value = the slowest rank's rate x N",
     }
+
+
+# ====================================================================== CPU end to end (C1)
+C1_SHAPE = dict(vocab_size=151936, hidden_size=896, intermediate_size=4864,
+                num_hidden_layers=24, num_attention_heads=14, num_key_value_heads=2,
+                rope_theta=1_000_000.0, tie_word_embeddings=True, max_position_embeddings=32768)
+C1_GOLDEN = REPO / "tests" / "golden" / "greedy_c1.json"
+
+
+def c1_model():
+    """Random-init Qwen2.5-0.5B architecture, fp32, initialised on the CPU from
+    torch.manual_seed(0) (the weights the reference engine's golden tokens came from)."""
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    cfg = Qwen2Config(**C1_SHAPE, attn_implementation="sdpa")
+    torch.manual_seed(0)
+    return Qwen2ForCausalLM(cfg).eval()
+
+
+def _c1_run(runner, golden, device: str) -> tuple[dict, int]:
+    from llm_engineering_b200 import engine as eng
+
+    cfg = eng.EngineConfiguration(device=device, block_size=16, num_blocks=2048,
+                                  max_sequences=8, max_batched_tokens=2048, seed=0)
+    engine = eng.Engine(configuration=cfg, model_runner=runner)
+    for r in golden["requests"]:
+        engine.submit(eng.Request(request_id=r["request_id"], prompt_token_ids=tuple(r["prompt"]),
+                                  max_new_tokens=32, ignore_eos=True))
+    engine.run_until_complete()
+    tokens = {s.request.request_id: list(s.generated_token_ids) for s in engine.finished_sequences}
+    return tokens, sum(len(t) for t in tokens.values())
+
+
+def c1_section(run: Run, args) -> dict:
+    """The CPU end-to-end configuration run on the GPU: this package's engine +
+    B200PagedModelRunner, fp32 (CUDA-core attention kernels), 8 requests x 32 greedy
+    tokens; one step = one whole run of the 8 requests. The tokens are checked against the
+    reference engine's golden tokens."""
+    from llm_engineering_b200.runner import B200PagedModelRunner
+    from llm_engineering_b200.storage import PagedKVStorage
+
+    golden = json.loads(C1_GOLDEN.read_text())
+    tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        model = c1_model().to(run.dev)
+        storage = PagedKVStorage(24, 2048, 16, 2, 64, torch.float32, run.dev)
+        runner = B200PagedModelRunner(model, run.dev, storage)
+        tokens, n_tok = _c1_run(runner, golden, "cuda")
+        match = all(tokens[rid] == want for rid, want in golden["generated"].items())
+        for _ in range(args.warmup):
+            _c1_run(runner, golden, "cuda")
+        run.barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(run.stream)
+        for _ in range(args.steps):
+            _c1_run(runner, golden, "cuda")
+        t1.record(run.stream)
+        torch.cuda.synchronize(run.dev)
+        run.barrier()
+        (ms,) = run.max(t0.elapsed_time(t1))
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = tf32
+    return {
+        "metric": "generated tok/s (engine + B200PagedModelRunner, random-init Qwen2.5-0.5B, "
+                  "fp32, 8 requests x 32 greedy tokens)",
+        "value": round(n_tok * args.steps * run.world / (ms / 1e3), 1), "unit": "tok/s",
+        "steps": args.steps, "ms_per_step": round(ms / args.steps, 3), "dtype": "f32",
+        "data": "the configuration-1 requests (prompts of 16..128 ids from random.Random(0))",
+        "config": {"workload": "8 requests, 32 greedy tokens each, block 16, 2048-block pool, "
+                               "24 layers, 14/2 heads, head_dim 64, vocab 151936",
+                   "step": "one whole run of the 8 requests (32 engine steps)"},
+        "tokens_match_reference_engine": match,
+    }
+
+
+def cpu_c1_baseline() -> dict:
+    """The configuration-1 run on the host cores, fp32, through this package's engine and
+    the oracle's restatement of the reference's PagedModelRunner (gather + dense mask +
+    SDPA); one whole run of the 8 requests."""
+    from oracle.runner import ReferencePackedRunner
+
+    golden = json.loads(C1_GOLDEN.read_text())
+    model = c1_model()
+    shape = (24, 2048 * 16, 2, 64)
+    runner = ReferencePackedRunner(model, torch.zeros(shape), torch.zeros(shape), 16)
+    t = time.perf_counter()
+    tokens, n_tok = _c1_run(runner, golden, "cpu")
+    dt = time.perf_counter() - t
+    match = all(tokens[rid] == want for rid, want in golden["generated"].items())
+    return {"value": round(n_tok / dt, 2), "unit": "tok/s", "cores": torch.get_num_threads(),
+            "kind": "port", "tokens_match_reference_engine": match,
+            "sample": "one whole configuration-1 run (8 requests x 32 tokens), fp32"}
 
 
 # ====================================================================== CPU baselines
@@ -1177,9 +1307,13 @@ def run_default(args) -> None:
         line["gpu_launches_total"] = (line["gpu_launches"] + line["prefill"]["gpu_launches"]
                                       + line["longctx"]["gpu_launches"]
                                       + line["model"]["gpu_launches"])
+        line["c1"] = c1_section(run, args)
+        torch.cuda.empty_cache()
     if run.rank == 0:
         if run.world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
+            if "c1" in line:
+                line["c1"]["cpu_baseline"] = cpu_c1_baseline()
         print(json.dumps(line), flush=True)
     run.close()
 
@@ -1230,7 +1364,7 @@ def run_mixed(args) -> None:
     torch.cuda.empty_cache()
     engine, _ = mixed_engine(run.dev, model)
     run.barrier()
-    line["offered_load"] = offered_load(run, engine, RequestStream(1000 + run.rank),
+    line["offered_load"] = offered_load(run, engine, RequestStream(1000, run.rank, run.world),
                                         args.duration)
     run.barrier()
     if run.rank == 0:
@@ -1346,6 +1480,10 @@ def main() -> None:
                     help="skip the sustained window and the long-context e2e leg")
     ap.add_argument("--duration", type=float, default=30.0,
                     help="seconds of Poisson arrivals in --workload mixed")
+    ap.add_argument("--mix-warmup", type=int, default=None,
+                    help="engine warm-up steps (default: enough to prefill the first prompts)")
+    ap.add_argument("--mix-steps", type=int, default=None,
+                    help="timed engine steps (default: max(--steps, 100))")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -1,9 +1,11 @@
 """Generate the golden fixtures by running the reference engine itself.
 
-Run in a container where the reference project is mounted (it is imported from
-``/root/reference``; nothing at test time reads it):
+Run where the reference project is checked out (it is imported from the path given;
+nothing at test time reads it):
 
-    python tests/golden/make_golden.py [--skip-greedy]
+    python tests/golden/make_golden.py --reference PATH [--skip-greedy]
+
+(``LLM_ENGINEERING_REFERENCE`` may give the path instead of ``--reference``.)
 
 Fixtures written next to this script:
   storage_roundtrip.npz  PagedKVStorage.scatter/gather on non-contiguous slots, 3 layers
@@ -22,6 +24,7 @@ from __future__ import annotations
 import argparse
 import hashlib
 import json
+import os
 import random
 import sys
 from pathlib import Path
@@ -29,7 +32,19 @@ from pathlib import Path
 import numpy as np
 import torch
 
-REF = Path("/root/reference")
+
+def _reference_root() -> Path:
+    ap = argparse.ArgumentParser(add_help=False)
+    ap.add_argument("--reference")
+    known, _ = ap.parse_known_args()
+    root = known.reference or os.environ.get("LLM_ENGINEERING_REFERENCE")
+    if not root:
+        sys.exit("make_golden.py: pass --reference PATH (the reference project's checkout) "
+                 "or set LLM_ENGINEERING_REFERENCE")
+    return Path(root)
+
+
+REF = _reference_root()
 OUT = Path(__file__).resolve().parent
 sys.path.insert(0, str(REF))
 
@@ -375,6 +390,7 @@ def make_greedy_c1() -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", help="the reference project's checkout")
     ap.add_argument("--skip-greedy", action="store_true")
     args = ap.parse_args()
     make_storage_roundtrip()
