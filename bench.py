@@ -73,13 +73,15 @@ sys.path.insert(0, str(REPO))
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of K2 on the
 # decode workload (append mode: the KV write fused in), from one ncu capture of a K2 launch
-# over the same sequences and block tables: 616.60 MB read + 7.20 MB written.
-K2_TRAFFIC_BYTES: float | None = 623.803904e6
+# over the same sequences and block tables: 616.68 MB read + 7.28 MB written.
+K2_TRAFFIC_BYTES: float | None = 623.967232e6
 # The same for K3 on the 32-prompt prefill workload, from one ncu capture of a K3 launch:
 # 211.81 MB read + 117.18 MB written.
 K3_TRAFFIC_BYTES: float | None = 328.994816e6
-# The same for K2 on the long-context workload (one-layer pool, same tables).
-LC_K2_TRAFFIC_BYTES: float | None = None
+# The same for K2 on the long-context workload, from a capture over a one-layer pool with
+# the same sequences and tables (per-launch traffic does not depend on the pool's layer
+# count): 2,599.38 MB read + 9.10 MB written.
+LC_K2_TRAFFIC_BYTES: float | None = 2.608486e9
 # Prompt groups of the prefill e2e leg (copies of one group overlap another's compute).
 E2E_GROUPS = 4
 SUSTAIN_S = 2.0  # length of the sustained-clock window after the timed region
@@ -760,8 +762,11 @@ MIX_DECODES, MIX_SLICES, MIX_SLICE = 192, 4, 512
 MIX_PROMPT_LO, MIX_PROMPT_HI, MIX_OUT = 128, 2048, 256
 MIX_BLOCKS = 32768      # 524,288 slots: room for 196 sequences of 2,048 + 256 tokens
 MIX_RATE = 20.0         # requests/s per GPU in the offered-load run
-MIX_WARMUP_STEPS = 110  # prefill of the first 196 prompts (~213k tokens at 2,048 a step)
-MIX_TIMED_STEPS = 100
+# The first ~110 steps prefill the first 196 prompts (~213k tokens at 2,048 a step); the
+# prefill load then swings with the waves of completions (480 to 1,200 prefill tokens a
+# step over 100-step windows, ~800 on average), so the timed window is long.
+MIX_WARMUP_STEPS = 200
+MIX_TIMED_STEPS = 300
 MIX_PROBE_STEPS = 20
 
 
@@ -1483,7 +1488,7 @@ def main() -> None:
     ap.add_argument("--mix-warmup", type=int, default=None,
                     help="engine warm-up steps (default: enough to prefill the first prompts)")
     ap.add_argument("--mix-steps", type=int, default=None,
-                    help="timed engine steps (default: max(--steps, 100))")
+                    help="timed engine steps (default: max(--steps, 300))")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
