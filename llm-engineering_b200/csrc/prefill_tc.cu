@@ -266,48 +266,11 @@ __device__ __forceinline__ float row_max64(const uint32_t (&r0)[32], const uint3
   return fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
 }
 
-// 2^x of a pair of fp32 values on the FMA and integer pipes, leaving the MUFU unit (whose
-// 16 ex2 per clock per SM the two heads' softmaxes otherwise queue on) to the other pairs.
-// Cody-Waite range reduction: j = floor(x) from an add of 1.5 * 2^23 rounded toward -inf
-// (its low mantissa bits then hold j), f = x - j in [0, 1); 2^f from a degree-3 polynomial
-// with p(0) = 1, whose coefficients were fit for this kernel by iteratively reweighted
-// least squares on the relative error over [0, 1) (maximum relative error 8.7e-5, below the
-// 16-bit rounding of P); 2^j is added to the exponent field as the integer j << 23 (the
-// magic's own bits shift out). x is clamped to [-127, 127]: below, P underflows anyway;
-// above, the result stays finite and large, so the row-sum check still catches the row.
-constexpr float kExp2C1 = 0.6951148f;
-constexpr float kExp2C2 = 0.22765392f;
-constexpr float kExp2C3 = 0.07705885f;
-constexpr float kExp2Magic = 12582912.0f;  // 1.5 * 2^23
-
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fminf(fmaxf(x, -127.f), 127.f);
-  float t;
-  asm("add.rm.f32 %0, %1, 0f4B400000;" : "=f"(t) : "f"(x));  // 1.5 * 2^23 + floor(x)
-  const float fr = x - (t - kExp2Magic);                      // x - floor(x), exact
-  const float p = fmaf(fmaf(fmaf(kExp2C3, fr, kExp2C2), fr, kExp2C1), fr, 1.f);
-  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
-}
-
-__device__ __forceinline__ void exp2_fma_pair(uint64_t x, float& e0, float& e1) {
-  float x0, x1;
-  f2unpack(x, x0, x1);
-  e0 = exp2_fma(x0);
-  e1 = exp2_fma(x1);
-}
-
-// Pairs of a 64-key half whose exp2 runs on the FMA pipe (kFmaExpPairs of every 8).
-#ifndef B2P_FMA_EXP_PAIRS
-#define B2P_FMA_EXP_PAIRS 0
-#endif
-constexpr int kFmaExpPairs = B2P_FMA_EXP_PAIRS;
-__device__ __forceinline__ constexpr bool fma_exp_pair(int q) {
-  return ((q & 7) * kFmaExpPairs) / 8 != (((q & 7) + 1) * kFmaExpPairs) / 8;
-}
-
 // P = exp2(S * scale_log2 - m) of a 64-key row, packed in pairs for tcgen05.st; returns
-// the row sum. kMasked: keys at or past `nvis` get 0. kFmaExpPairs of every 8 pairs take
-// exp2_fma_pair, spread evenly, the rest the MUFU unit.
+// the row sum. kMasked: keys at or past `nvis` get 0. (Computing 1 to 3 of every 8 pairs'
+// exp2 on the FMA pipe instead, by range reduction and a cubic, was measured slower: 791 to
+// 964 us per launch against 714 on the 32-prompt workload. The softmax is bound by
+// instruction issue and latency, not by MUFU throughput.)
 template <typename T, bool kMasked>
 __device__ __forceinline__ float row_exp64(const uint32_t (&r0)[32], const uint32_t (&r1)[32],
                                            int nvis, float scale_log2, float m,
@@ -320,15 +283,10 @@ __device__ __forceinline__ float row_exp64(const uint32_t (&r0)[32], const uint3
     const uint32_t* r = q < 16 ? r0 : r1;
     const int c = (q & 15) * 2;
     const uint64_t x = ffma2(f2pack(__uint_as_float(r[c]), __uint_as_float(r[c + 1])), sc, nm);
-    float e0, e1;
-    if (fma_exp_pair(q)) {
-      exp2_fma_pair(x, e0, e1);
-    } else {
-      float x0, x1;
-      f2unpack(x, x0, x1);
-      e0 = fast_exp2(x0);
-      e1 = fast_exp2(x1);
-    }
+    float x0, x1, e0, e1;
+    f2unpack(x, x0, x1);
+    e0 = fast_exp2(x0);
+    e1 = fast_exp2(x1);
     if (kMasked) {
       e0 = 2 * q < nvis ? e0 : 0.f;
       e1 = 2 * q + 1 < nvis ? e1 : 0.f;

@@ -42,7 +42,8 @@ _PREEMPTIBLE_FROM = frozenset({SequenceStatus.RUNNING})
 class SequenceState:
     """Token history and lifecycle of one request."""
 
-    __slots__ = ("request", "_buf", "_prompt_len", "_len", "status", "finish_reason")
+    __slots__ = ("request", "_buf", "_prompt_len", "_len", "status", "finish_reason",
+                 "admissions")
 
     def __init__(self, request: Request, generated_token_ids=(),
                  status: SequenceStatus = SequenceStatus.WAITING,
@@ -58,6 +59,9 @@ class SequenceState:
         self._buf[self._prompt_len:self._len] = gen
         self.status = SequenceStatus(status)
         self.finish_reason = None if finish_reason is None else FinishReason(finish_reason)
+        # Times the sequence was admitted to run: its block table is only ever appended to
+        # between two admissions (a preemption frees it, the next admission allocates anew).
+        self.admissions = 0
 
     # ------------------------------------------------------------------ token history
     @property
@@ -106,6 +110,7 @@ class SequenceState:
         if self.status not in _RUNNABLE_FROM:
             raise RuntimeError("Only a waiting or preempted sequence can be marked running.")
         self.status = SequenceStatus.RUNNING
+        self.admissions += 1
 
     def mark_preempted(self) -> None:
         if self.status not in _PREEMPTIBLE_FROM:

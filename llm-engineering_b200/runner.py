@@ -182,6 +182,63 @@ def _storage_of(paged_cache) -> Any:
     return getattr(paged_cache, "storage", paged_cache)
 
 
+class _TableMirror:
+    """Device-resident copy of the block tables of the sequences a step runs, one row per
+    (request, admission), updated with only the blocks each table gained since its last
+    step (the engine appends to a table between admissions and never rewrites it). Rows of
+    sequences a step does not run are released; a sequence that comes back gets a fresh
+    row and a whole upload. Per step this moves a few bytes per new block instead of the
+    whole [B, W] table, and the host walks only the new blocks."""
+
+    def __init__(self, device: torch.device, rows: int = 256, cols: int = 64) -> None:
+        self.device = device
+        self.table = torch.full((rows, cols), -1, dtype=torch.int32, device=device)
+        self._rows: dict[object, list[int]] = {}  # key -> [row, blocks uploaded]
+        self._free = list(range(rows - 1, -1, -1))
+
+    def _grow(self, rows: int, cols: int) -> None:
+        old = self.table
+        self.table = torch.full((rows, cols), -1, dtype=torch.int32, device=self.device)
+        self.table[:old.shape[0], :old.shape[1]] = old
+        self._free = list(range(rows - 1, old.shape[0] - 1, -1)) + self._free
+
+    def sync(self, keys: Sequence, block_lists: Sequence) -> list[int]:
+        """Rows of `keys` (one per execution), after uploading their new blocks."""
+        live = set(keys)
+        for key in [k for k in self._rows if k not in live]:
+            self._free.append(self._rows.pop(key)[0])
+        need_cols = max(len(b) for b in block_lists)
+        need_rows = len(self._rows) + sum(1 for k in live if k not in self._rows)
+        rows_cap, cols_cap = self.table.shape
+        while rows_cap < need_rows:
+            rows_cap *= 2
+        while cols_cap < need_cols:
+            cols_cap *= 2
+        if (rows_cap, cols_cap) != tuple(self.table.shape):
+            self._grow(rows_cap, cols_cap)
+        stride = self.table.shape[1]
+        rows, idx, vals = [], [], []
+        for key, blocks in zip(keys, block_lists, strict=True):
+            entry = self._rows.get(key)
+            if entry is None:
+                entry = [self._free.pop(), 0]
+                self._rows[key] = entry
+            row, done = entry
+            if len(blocks) > done:
+                base = row * stride
+                idx.extend(range(base + done, base + len(blocks)))
+                vals.extend(blocks[done:])
+                entry[1] = len(blocks)
+            rows.append(row)
+        if idx:
+            packed = torch.from_numpy(np.asarray([idx, vals], dtype=np.int64))
+            if self.device.type == "cuda":
+                packed = packed.pin_memory()
+            packed = packed.to(self.device, non_blocking=True)
+            self.table.view(-1).index_copy_(0, packed[0], packed[1].to(torch.int32))
+        return rows
+
+
 class B200PagedModelRunner:
     """``ModelRunner`` implementation running the packed forward on the paged kernels.
 
@@ -214,6 +271,7 @@ class B200PagedModelRunner:
         self._head_dim = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
         self._workspace = torch.zeros(16, dtype=torch.uint8, device=self._device)
         self._err = torch.zeros(1, dtype=torch.int32, device=self._device)
+        self._mirror: _TableMirror | None = None
 
     # ------------------------------------------------------------------ host metadata
     @staticmethod
@@ -234,6 +292,10 @@ class B200PagedModelRunner:
 
     def _describe(self, executions: Sequence) -> dict:
         bs = self._storage.block_size
+        # Executions of this package's engine (block lists, sequences that count their
+        # admissions) keep their tables in the device mirror, updated with new blocks only.
+        mirrored = all(getattr(ex, "block_ids", None) is not None
+                       and hasattr(ex.sequence, "admissions") for ex in executions)
         phases, qlens, lengths, tables, is_slots, token_parts = [], [], [], [], [], []
         for ex in executions:
             phase = _phase_of(ex)
@@ -253,7 +315,7 @@ class B200PagedModelRunner:
                     blocks = cand
                 else:  # not block-structured: keep the per-position slots
                     blocks, slot_list = slots, True
-            tables.append(np.asarray(blocks, dtype=np.int64))
+            tables.append(blocks if mirrored else np.asarray(blocks, dtype=np.int64))
             is_slots.append(slot_list)
             token_parts.append(self._token_ids(ex.sequence, length - qlen, length))
             phases.append(phase)
@@ -269,7 +331,7 @@ class B200PagedModelRunner:
                     expanded.append(t[pos // bs] * bs + pos % bs)
             tables, bs = expanded, 1
         return {"phases": phases, "qlens": qlens, "lengths": lengths, "tables": tables,
-                "tokens": np.concatenate(token_parts), "block_size": bs}
+                "tokens": np.concatenate(token_parts), "block_size": bs, "mirrored": mirrored}
 
     def _build_batch(self, executions: Sequence) -> tuple[StepBatch, torch.Tensor]:
         d = self._describe(executions)
@@ -278,14 +340,27 @@ class B200PagedModelRunner:
         num_decode = 0
         while num_decode < n and d["phases"][num_decode] == DECODE:
             num_decode += 1
-        width = max(1, max(len(t) for t in d["tables"]))
-        host = np.full((3 * n + n * width,), -1, dtype=np.int32)
+        kernels = _ops
+        bs = d["block_size"]
+        if d["mirrored"]:
+            # rows of the device mirror (new blocks uploaded by sync); K4 gathers this step's
+            # padded [n, width] tables from them
+            keys = [(ex.sequence.request.request_id, ex.sequence.admissions) for ex in executions]
+            if self._mirror is None:
+                self._mirror = _TableMirror(dev)
+            mirror_rows = self._mirror.sync(keys, d["tables"])
+            width = max(1, max(-(-length // bs) for length in d["lengths"]))
+            host = np.empty((3 * n,), dtype=np.int32)
+            host[2 * n:3 * n] = mirror_rows
+        else:
+            width = max(1, max(len(t) for t in d["tables"]))
+            host = np.full((3 * n + n * width,), -1, dtype=np.int32)
+            host[2 * n:3 * n] = np.arange(n, dtype=np.int32)
+            tab = host[3 * n:].reshape(n, width)
+            for i, t in enumerate(d["tables"]):
+                tab[i, :len(t)] = t
         host[0:n] = d["qlens"]
         host[n:2 * n] = d["lengths"]
-        host[2 * n:3 * n] = np.arange(n, dtype=np.int32)
-        tab = host[3 * n:].reshape(n, width)
-        for i, t in enumerate(d["tables"]):
-            tab[i, :len(t)] = t
         staged = torch.from_numpy(host)
         tokens = torch.from_numpy(d["tokens"])
         if dev.type == "cuda":
@@ -296,11 +371,14 @@ class B200PagedModelRunner:
         qlens = dev_i32[0:n]
         ctx = dev_i32[n:2 * n]
         rows = dev_i32[2 * n:3 * n]
-        tables = dev_i32[3 * n:].view(n, width)
         total_q = int(sum(d["qlens"]))
-        kernels = _ops
-        md = kernels.build_metadata(qlens, ctx, rows, tables, d["block_size"], total_q, 0,
-                                    self._err)
+        if d["mirrored"]:
+            md = kernels.build_metadata(qlens, ctx, rows, self._mirror.table, bs, total_q, width,
+                                        self._err)
+            tables = md["block_tables"]
+        else:
+            tables = dev_i32[3 * n:].view(n, width)
+            md = kernels.build_metadata(qlens, ctx, rows, tables, bs, total_q, 0, self._err)
         need = kernels.decode_workspace_size(max(num_decode, 1), self._hq, self._hkv,
                                              self._head_dim)
         if self._workspace.numel() < need:

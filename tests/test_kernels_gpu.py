@@ -206,12 +206,13 @@ def test_decode_workspace_sizes(ops):
     ctx = np.random.default_rng(91).integers(1, 4000, size=400).tolist()
     full = ops.decode_workspace_size(len(ctx), 12, 2, 128)
     accepted = 0
-    for shift in range(0, 8):
-        ws = torch.zeros(max(full >> shift, 16), dtype=torch.uint8, device=dev)
+    for size in (2 * full, full, full - 64, full // 2, full // 16):
+        ws = torch.zeros(max(size, 16), dtype=torch.uint8, device=dev)
         try:
             out, expect = _decode_case(ops, ctx, 90, workspace=ws)
         except ValueError as exc:
             assert "workspace" in str(exc).lower()
+            assert size < full
             continue
         accepted += 1
         close(out, expect, torch.bfloat16)

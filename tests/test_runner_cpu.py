@@ -82,13 +82,19 @@ class CpuKernels:
             p = np.arange(ki - qi, ki)
             pos.append(p)
             slots.append(table.numpy()[p // bs].astype(np.int64) * bs + p % bs)
+        # padded per-execution tables gathered from the mirror rows (-1 past each need)
+        width = max(max_blocks, 1)
+        bt = torch.full((len(q), width), -1, dtype=torch.int32)
+        for i, ki in enumerate(k):
+            nblk = min(-(-ki // bs), width, mirror.shape[1])
+            bt[i, :nblk] = mirror[int(rows[i]), :nblk]
         return {
             "cu_seqlens_q": torch.from_numpy(cu_q),
             "cu_seqlens_k": torch.from_numpy(cu_k),
             "positions": torch.from_numpy(np.concatenate(pos).astype(np.int64)),
             "slot_mapping": torch.from_numpy(np.concatenate(slots).astype(np.int32)),
             "logit_indices": torch.from_numpy((cu_q[1:] - 1).astype(np.int64)),
-            "block_tables": mirror,
+            "block_tables": bt,
         }
 
 
@@ -206,3 +212,35 @@ def test_runner_rejects_empty_batch():
 class _Storage:
     def __init__(self, kc, vc, bs):
         self.key_cache, self.value_cache, self.block_size = kc, vc, bs
+
+
+def test_block_table_mirror_tracks_appends_readmissions_and_growth():
+    """The runner's device mirror of block tables, driven by a random step sequence: tables
+    that grow by appended blocks, sequences that leave and come back under a new admission
+    with new blocks, more rows and columns than the first allocation. After every step each
+    live row must hold exactly its sequence's block list."""
+    from llm_engineering_b200.runner import _TableMirror
+
+    rng = np.random.default_rng(17)
+    mirror = _TableMirror(torch.device("cpu"), rows=4, cols=2)
+    tables: dict[tuple[str, int], list[int]] = {}
+    admissions = {f"r{i}": 1 for i in range(40)}
+    next_block = 0
+    for _ in range(200):
+        running = [f"r{i}" for i in rng.choice(40, size=int(rng.integers(1, 12)), replace=False)]
+        keys, lists = [], []
+        for rid in running:
+            if rng.random() < 0.1:  # preempted and re-admitted: a new table
+                admissions[rid] += 1
+            key = (rid, admissions[rid])
+            t = tables.setdefault(key, [])
+            for _ in range(int(rng.integers(0, 3)) + (0 if t else 1)):
+                t.append(next_block)
+                next_block += 1
+            keys.append(key)
+            lists.append(tuple(t))
+        rows = mirror.sync(keys, lists)
+        assert len(set(rows)) == len(rows)
+        for row, blocks in zip(rows, lists):
+            assert mirror.table[row, :len(blocks)].tolist() == list(blocks)
+    assert mirror.table.shape[0] >= 12 and mirror.table.shape[1] > 2
