@@ -9,8 +9,9 @@
 //
 //   S = Q K^T   tcgen05.mma kind::f16, A = Q (smem, K-major), B = K tile (smem, K-major),
 //               D = S in tensor memory (fp32, 128 lanes x 128 columns, one per head)
-//   P = softmax rows of S, one thread per query row (tcgen05.ld -> fp32 -> exp2), written
-//       back as bf16/f16 (tcgen05.st) over the second half of its own S columns (head_dim
+//   P = softmax rows of S, two threads per query row (two warps share a TMEM lane
+//       quarter, one per 64-key half of the tile: tcgen05.ld -> fp32 -> exp2), written back
+//       as bf16/f16 (tcgen05.st) over the first 32 of each half's own 64 S columns (head_dim
 //       128) or into columns of its own (head_dim 64)
 //   O += P V    tcgen05.mma with A = P from tensor memory, B = V tile (smem, MN-major),
 //               D = O in tensor memory (fp32, 128 x head_dim, one per head)
@@ -26,13 +27,19 @@
 // prefill when q_len == ctx, chunked prefill otherwise). The first KV tile of an item sets
 // each row's reference max; later tiles take exp2 against that reference in one pass (the
 // row sum flags the rare rows whose scores outgrow it by more than 2^8, which then move
-// the reference and rescale O, l and the P already stored). The softmax is bound by
-// neither exp2 throughput nor its tensor-memory loads but is sensitive to issue slots on
-// its SM sub-partition, so the exponent arithmetic runs as packed f32x2 FMA/ADD.
+// the reference and rescale O and l before any P of the tile is stored). The two warps of a
+// row agree on its reference max, on a move of it and on aborts through shared memory, at
+// one 64-thread named barrier per tile. One softmax warp per row ran alone on its SM
+// sub-partition while the other head waited, latency-bound; two warps per row there were
+// measured 5.4 % faster (673.7 against 712.2 us per launch on the 32-prompt workload). The
+// softmax is bound by neither exp2 throughput nor its tensor-memory loads, and the
+// exponent arithmetic runs as packed f32x2 FMA/ADD.
 //
-// Warp roles (320 threads): warp 0 = TMA producer and work-item scheduler, warp 1 =
-// tensor-memory owner and MMA issuer (one thread), warps 2..5 = softmax + epilogue of head
-// A, warps 6..9 = the same for head B (thread = TMEM lane = query row).
+// Warp roles (576 threads): warp 0 = TMA producer and work-item scheduler, warp 1 =
+// tensor-memory owner and MMA issuer (one thread), warps 2..9 = softmax + epilogue of head
+// A, warps 10..17 = the same for head B. Softmax warp w serves TMEM lanes 32 * (w % 4)
+// .. +31 (thread = lane = query row), keys 0..63 of each tile for w - 2 in {0..3, 8..11},
+// keys 64..127 otherwise.
 #include <atomic>
 #include <mutex>
 #include <type_traits>
@@ -45,12 +52,12 @@ using namespace b2p;
 
 constexpr int kM = 128;     // query rows per tile
 constexpr int kN = 128;     // keys per KV tile
-constexpr int kSeqCache = 1024;   // scheduler tables: sequences cached in shared memory
+constexpr int kSeqCache = 512;    // scheduler tables: sequences cached in shared memory
 constexpr int kSizeCache = 1024;  // ... and tile sizes (KV tiles per query tile)
-constexpr int kThreads = 320;
+constexpr int kThreads = 576;
 constexpr int kSub = 16;
 constexpr int kSubPerTile = kN / kSub;
-constexpr int kConsumerWarps = 9;  // the MMA issuer and eight softmax warps
+constexpr int kConsumerWarps = 17;  // the MMA issuer and sixteen softmax warps
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct PrefillParams {
@@ -88,9 +95,13 @@ struct Plan {
                                        // s_read[2] (by head; head_dim 64)
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kOffItems = kOffMisc + 64;
-  // epilogue staging: 8 warps x 32 rows x 64 B
+  // epilogue staging: 16 warps x 32 rows x 32 B
   static constexpr int kOffStage = (kOffItems + 2 * 48 + 127) / 128 * 128;
-  static constexpr int kOffSched = kOffStage + 8 * 32 * 64;  // scheduler tables
+  // row exchange between the two warps of a lane quarter: 8 pairs x [2 parity][2 half]
+  // x (32 floats), then 8 pairs x [2 parity][2 half] flags
+  static constexpr int kOffXch = kOffStage + 16 * 32 * 32;
+  static constexpr int kOffXok = kOffXch + 8 * 4 * 32 * 4;
+  static constexpr int kOffSched = kOffXok + 8 * 4 * 4;  // scheduler tables
   static constexpr int kSmemBytes = kOffSched + (3 * kSeqCache + kSizeCache + 1) * 4;
 };
 
@@ -107,6 +118,18 @@ __device__ __forceinline__ uint32_t col_o(int h) {
 template <int D>
 __device__ __forceinline__ uint32_t col_p(int h) {
   return D == 64 ? 384u + 64u * h : col_s(h) + 64u;
+}
+// TMEM column of P for keys 16*kk .. 16*kk+15 (two keys per column). head_dim 64: P has 64
+// columns of its own. head_dim 128: the softmax warp of key half `half` stores its 64 keys'
+// P over the first 32 columns of its own 64 S columns (keys 0..63 at S + 0, keys 64..127 at
+// S + 64), which it alone has read.
+template <int D>
+__device__ __forceinline__ uint32_t col_p_keys(int h, int kk) {
+  return D == 64 ? col_p<D>(h) + 8u * kk : col_s(h) + (kk < 4 ? 8u * kk : 64u + 8u * (kk - 4));
+}
+template <int D>
+__device__ __forceinline__ uint32_t col_p_half(int h, int half) {
+  return D == 64 ? col_p<D>(h) + 32u * half : col_s(h) + 64u * half;
 }
 
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -246,50 +269,43 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// Row max of a 64-key S tile (columns 0..31 in r0, 32..63 in r1), four independent
-// three-input max chains. kMasked: keys at or past `nvis` are ignored.
+// Row max of 32 S columns (keys base .. base+31 of the row's visible range), two chains.
 template <bool kMasked>
-__device__ __forceinline__ float row_max64(const uint32_t (&r0)[32], const uint32_t (&r1)[32],
-                                           int nvis) {
-  float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
-  auto v = [&](const uint32_t (&r)[32], int base, int c) {
-    const float x = __uint_as_float(r[c]);
-    return (!kMasked || base + c < nvis) ? x : -INFINITY;
-  };
+__device__ __forceinline__ float row_max32(const uint32_t (&r)[32], int base, int nvis) {
+  float a0 = -INFINITY, a1 = -INFINITY;
 #pragma unroll
   for (int c = 0; c < 32; c += 4) {
-    a0 = fmax3(a0, v(r0, 0, c), v(r0, 0, c + 1));
-    a1 = fmax3(a1, v(r0, 0, c + 2), v(r0, 0, c + 3));
-    a2 = fmax3(a2, v(r1, 32, c), v(r1, 32, c + 1));
-    a3 = fmax3(a3, v(r1, 32, c + 2), v(r1, 32, c + 3));
+    auto v = [&](int cc) {
+      const float x = __uint_as_float(r[cc]);
+      return (!kMasked || base + cc < nvis) ? x : -INFINITY;
+    };
+    a0 = fmax3(a0, v(c), v(c + 1));
+    a1 = fmax3(a1, v(c + 2), v(c + 3));
   }
-  return fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
+  return fmaxf(a0, a1);
 }
 
-// P = exp2(S * scale_log2 - m) of a 64-key row, packed in pairs for tcgen05.st; returns
-// the row sum. kMasked: keys at or past `nvis` get 0. (Computing 1 to 3 of every 8 pairs'
-// exp2 on the FMA pipe instead, by range reduction and a cubic, was measured slower: 791 to
-// 964 us per launch against 714 on the 32-prompt workload. The softmax is bound by
-// instruction issue and latency, not by MUFU throughput.)
+// P of 32 S columns (keys base .. base+31) into pk[16] (two keys per word); returns their sum.
+// (Computing 1 to 3 of every 8 pairs' exp2 on the FMA pipe instead, by range reduction and a
+// cubic, was measured slower: 791 to 964 us per launch against 714 with one softmax warp
+// per row: the softmax is not bound by MUFU throughput.)
 template <typename T, bool kMasked>
-__device__ __forceinline__ float row_exp64(const uint32_t (&r0)[32], const uint32_t (&r1)[32],
-                                           int nvis, float scale_log2, float m,
-                                           uint32_t (&pk)[32]) {
+__device__ __forceinline__ float row_exp32(const uint32_t (&r)[32], int base, int nvis,
+                                           float scale_log2, float m, uint32_t* pk) {
   const uint64_t sc = f2pack(scale_log2, scale_log2);
   const uint64_t nm = f2pack(-m, -m);
   uint64_t acc0 = f2pack(0.f, 0.f), acc1 = f2pack(0.f, 0.f);
 #pragma unroll
-  for (int q = 0; q < 32; ++q) {  // pair q: keys 2q, 2q+1 (r0 for q < 16, r1 after)
-    const uint32_t* r = q < 16 ? r0 : r1;
-    const int c = (q & 15) * 2;
-    const uint64_t x = ffma2(f2pack(__uint_as_float(r[c]), __uint_as_float(r[c + 1])), sc, nm);
+  for (int q = 0; q < 16; ++q) {
+    const uint64_t x =
+        ffma2(f2pack(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1])), sc, nm);
     float x0, x1, e0, e1;
     f2unpack(x, x0, x1);
     e0 = fast_exp2(x0);
     e1 = fast_exp2(x1);
     if (kMasked) {
-      e0 = 2 * q < nvis ? e0 : 0.f;
-      e1 = 2 * q + 1 < nvis ? e1 : 0.f;
+      e0 = base + 2 * q < nvis ? e0 : 0.f;
+      e1 = base + 2 * q + 1 < nvis ? e1 : 0.f;
     }
     if (q & 1) acc1 = fadd2(acc1, f2pack(e0, e1)); else acc0 = fadd2(acc0, f2pack(e0, e1));
     pk[q] = pack2<T>(e0, e1);
@@ -298,20 +314,6 @@ __device__ __forceinline__ float row_exp64(const uint32_t (&r0)[32], const uint3
   f2unpack(acc0, s0, s1);
   f2unpack(acc1, s2, s3);
   return (s0 + s1) + (s2 + s3);
-}
-
-// P of a row half as stored (two 16-bit values per column) times a, in place.
-template <typename T>
-__device__ __forceinline__ uint32_t scale_pair(uint32_t v, float a);
-template <>
-__device__ __forceinline__ uint32_t scale_pair<__nv_bfloat16>(uint32_t v, float a) {
-  const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v));
-  return pack2<__nv_bfloat16>(f.x * a, f.y * a);
-}
-template <>
-__device__ __forceinline__ uint32_t scale_pair<__half>(uint32_t v, float a) {
-  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&v));
-  return pack2<__half>(f.x * a, f.y * a);
 }
 
 // Work items. Sequence s has ntiles(s) = ceil(q_len_s / 128) query tiles; its tile t
@@ -531,8 +533,8 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&p_full[s], kM);
-      mbar_init(&s_read[s], kM);
+      mbar_init(&p_full[s], 2 * kM);
+      mbar_init(&s_read[s], 2 * kM);
       mbar_init(&o_done[s], 1);
       mbar_init(&item_full[s], 1);
       mbar_init(&item_empty[s], kConsumerWarps);
@@ -748,11 +750,11 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
         };
         auto issue_pv = [&](int h, int64_t gg, bool first) {
           const uint32_t v_addr = smem_u32(smem + L::kOffV + (int)(gg & 1) * L::kKVBytes);
-          const uint32_t p_tmem = tbase + col_p<D>(h);
 #pragma unroll
           for (int kk = 0; kk < kN / 16; ++kk) {
             const uint64_t db = smem_desc_sw128(v_addr + kk * (16 * 128), kN * 128, 1024);
-            mma_ts(tbase + col_o<D>(h), p_tmem + kk * 8, db, id_pv, (!first || kk > 0) ? 1u : 0u);
+            mma_ts(tbase + col_o<D>(h), tbase + col_p_keys<D>(h, kk), db, id_pv,
+                   (!first || kk > 0) ? 1u : 0u);
           }
           mma_commit(&o_done[h]);
         };
@@ -852,19 +854,49 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
     }
   } else {
     // ---------------------------------------------------------------- softmax + epilogue
-    const int h = (warp - 2) >> 2;      // 0: head A, 1: head B
-    const int quarter = warp & 3;        // TMEM lanes 32*quarter .. +31
+    // Two warps per TMEM lane quarter and head: warp half 0 takes keys 0..63 of every KV
+    // tile, half 1 keys 64..127, so each SM sub-partition runs two softmax warps of a head
+    // at once. The pair agrees on each row's reference max (and on aborts) through shared
+    // memory at one 64-thread named barrier per tile, before either stores P.
+    const int local = warp - 2;
+    const int h = local >> 3;             // 0: head A, 1: head B
+    const int half = (local >> 2) & 1;    // key half of every tile
+    const int quarter = warp & 3;         // TMEM lanes 32*quarter .. +31
     const int row = quarter * 32 + lane;  // query row within the tile
+    const int pair = h * 4 + quarter;     // named barrier 1 + pair (ids 1..8)
     const uint32_t lane_base = tbase + ((uint32_t)(quarter * 32) << 16);
-    const uint32_t s_col = lane_base + col_s(h);
-    const uint32_t o_col = lane_base + col_o<D>(h);
-    const uint32_t p_col = lane_base + col_p<D>(h);
+    const uint32_t s_col = lane_base + col_s(h) + 64u * half;        // my 64 S columns
+    const uint32_t p_col = lane_base + col_p_half<D>(h, half);       // my 32 P columns
+    const uint32_t o_col = lane_base + col_o<D>(h) + (uint32_t)(D / 2) * half;  // D/2 O cols
+    float* xv = reinterpret_cast<float*>(smem + L::kOffXch) + pair * (4 * 32);
+    int* xo = reinterpret_cast<int*>(smem + L::kOffXok) + pair * 4;
+    int ex_n = 0;  // exchanges so far (the pair runs them in lock step)
+    // Publish v and this warp's status, wait for the partner, return its v; both_ok tells
+    // whether both warps are still fine (then both go on, else both leave: the pair always
+    // meets at the same barriers).
+    auto exchange = [&](float v, bool mine_ok, bool& both_ok) -> float {
+      const int par = ex_n & 1;
+      ++ex_n;
+      xv[(par * 2 + half) * 32 + lane] = v;
+      if (lane == 0) xo[par * 2 + half] = mine_ok ? 1 : 0;
+      asm volatile("bar.sync %0, 64;" ::"r"(1 + pair) : "memory");
+      const float pv = xv[(par * 2 + (half ^ 1)) * 32 + lane];
+      both_ok = mine_ok && xo[par * 2 + (half ^ 1)] != 0;
+      return pv;
+    };
     int64_t g = 0;  // K/V tiles of the items seen so far (V stage of the tail fix-up)
     int n = 0;      // tiles of this head so far (S, P and O barrier phases)
     bool ok = true;
-    for (int i = 0; ok; ++i) {
+    for (int i = 0;; ++i) {
       ItemInfo it;
-      if (!take_item(i, it)) break;
+      it.seq = -1;
+      const bool got = ok && take_item(i, it);
+      bool both = false;
+      (void)exchange(0.f, got, both);
+      if (!both) {
+        if (got || it.seq >= 0) *abort_flag = 1;  // left on the partner's failure
+        break;
+      }
       if (it.n_kv == 0) continue;
       if (h == 1 && it.qh_b < 0) {  // an odd group's last head: head A alone
         g += it.n_kv;
@@ -873,205 +905,194 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
       const int qh = h ? it.qh_b : it.qh_a;
       const bool valid_row = row < it.rows_valid;
       const int pos = it.pos0 + row;
-      float m = -INFINITY, l = 0.f;
+      float m = -INFINITY, l = 0.f;  // l: this warp's half of the row sum
+      bool left = false;             // the pair left the item together
       for (int j = 0; j < it.n_kv; ++j, ++g, ++n) {
-        if (ok && !mbar_wait_bounded(&s_full[h], (uint32_t)(n & 1), p.err)) ok = false;
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok || *abort_flag) {
+        bool okw = ok;
+        if (okw && !mbar_wait_bounded(&s_full[h], (uint32_t)(n & 1), p.err)) okw = false;
+        okw = __all_sync(0xffffffffu, okw) && !*abort_flag;
+        const int key0 = j * kN + 64 * half;
+        // key c of my half is visible iff key0 + c <= pos (then also < ctx); chunks that
+        // every row of the warp sees whole (all but the diagonal tiles) skip the masks
+        const int nv = valid_row ? pos - key0 + 1 : 0;
+        const bool whole0 = __all_sync(0xffffffffu, nv >= 32);
+        const bool whole1 = __all_sync(0xffffffffu, nv >= 64);
+        uint32_t r[32], pk[32];
+        auto load = [&](int c) {
+          tmem_ld32(s_col + 32u * c, r);
+          tmem_wait_ld();
+        };
+        auto max_chunk = [&](int c) -> float {
+          const bool w = c ? whole1 : whole0;
+          return w ? row_max32<false>(r, 32 * c, nv) : row_max32<true>(r, 32 * c, nv);
+        };
+        auto exp_chunk = [&](int c) -> float {
+          const bool w = c ? whole1 : whole0;
+          return w ? row_exp32<T, false>(r, 32 * c, nv, p.scale_log2, m, pk + 16 * c)
+                   : row_exp32<T, true>(r, 32 * c, nv, p.scale_log2, m, pk + 16 * c);
+        };
+        // the largest S * scale_log2 over my 64 keys (two loads of S, still in TMEM)
+        auto max_half = [&]() -> float {
+          load(0);
+          const float a = max_chunk(0);
+          load(1);
+          return fmaxf(a, max_chunk(1)) * p.scale_log2;
+        };
+        auto exps = [&]() -> float {
+          load(0);
+          const float a = exp_chunk(0);
+          load(1);
+          return a + exp_chunk(1);
+        };
+        float v = -INFINITY, rs = 0.f;
+        if (okw) {
+          tc_fence_after();
+          if (j == 0) {
+            v = max_half();  // the first tile of an item sets each row's reference max
+          } else {
+            // one pass with the running reference m. exp2(x - m) is exact for any
+            // reference as long as x = S * scale - m stays small; the sum of my 64 keys is
+            // at most 64 * 2^8 when every x <= 8 and above 2^8 when any x > 8 (or on
+            // overflow), so rows whose sum passes 2^8 look at their true max
+            rs = exps();
+            // tcgen05.ld is .sync.aligned: the whole warp loads S again when any row needs
+            // its max (never inside a per-row branch)
+            const bool look = !(rs <= 256.f);
+            if (__any_sync(0xffffffffu, look)) {
+              const float xm = max_half() - m;
+              if (look) v = xm;
+            }
+          }
+        }
+        const float pv = exchange(v, okw, both);
+        if (!both) {
           ok = false;
+          left = true;
           break;
         }
-        tc_fence_after();
-        const int key0 = j * kN;
-        // key c of this tile is visible iff key0 + c <= pos (then also < ctx). Halves that
-        // every row of the warp sees whole (all but the diagonal tiles) skip the masks.
-        const int nv0 = valid_row ? pos - key0 + 1 : 0;  // visible keys from column 0
-        const int nv1 = nv0 - 64;                        // ... from column 64
-        const bool whole0 = __all_sync(0xffffffffu, nv0 >= 64);
-        const bool whole1 = __all_sync(0xffffffffu, nv1 >= 64);
-        uint32_t r0[32], r1[32], pk[32];  // S of a 64-key half, its P
-        float rs1, rs0;
-        // O *= alpha (per row) once PV of the previous tile has landed; l follows.
-        auto rescale_o = [&](float alpha) -> bool {
-          if (!mbar_wait_bounded(&o_done[h], (uint32_t)((n - 1) & 1), p.err)) ok = false;
-          ok = __all_sync(0xffffffffu, ok);
-          if (!ok) return false;
-          tc_fence_after();
-          for (int c0 = 0; c0 < D; c0 += 16) {  // 16 columns at a time: S/P stay live
-            uint32_t o[16];
-            tmem_ld16(o_col + c0, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int c = 0; c < 16; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-            tmem_st16(o_col + c0, o);
-          }
-          tmem_wait_st();
-          l *= alpha;
-          return true;
-        };
-        auto exp_half = [&](bool whole, int nv) -> float {
-          return whole ? row_exp64<T, false>(r0, r1, nv, p.scale_log2, m, pk)
-                       : row_exp64<T, true>(r0, r1, nv, p.scale_log2, m, pk);
-        };
-        // Largest S * scale_log2 - m over the visible keys of the half in r0/r1.
-        auto xmax_half = [&](bool whole, int nv) -> float {
-          const float mx = whole ? row_max64<false>(r0, r1, nv) : row_max64<true>(r0, r1, nv);
-          return mx * p.scale_log2 - m;
-        };
-        // head_dim 64 (P has its own columns): the whole S is in registers, so the MMA warp
-        // may overwrite it with the next tile's QK^T; and P may only be stored once the
-        // previous tile's PV has read the P before it.
-        auto s_done = [&]() {
-          if constexpr (D == 64) {
-            tc_fence_before();
-            mbar_arrive(&s_read[h]);
-          }
-        };
-        auto p_writable = [&]() -> bool {
-          if constexpr (D == 64) {
-            if (n > 0 && ok && !mbar_wait_bounded(&o_done[h], (uint32_t)((n - 1) & 1), p.err))
-              ok = false;
-            ok = __all_sync(0xffffffffu, ok);
-            if (ok) tc_fence_after();
-          }
-          return ok;
-        };
+        bool step_ok = true;
         if (j == 0) {
-          // First tile of the item: the reference max comes from the tile (two passes; keys
-          // 64..127 are left in registers, their columns then take their P).
-          tmem_ld32(s_col, r0);
-          tmem_ld32(s_col + 32, r1);
-          tmem_wait_ld();
-          float mx = whole0 ? row_max64<false>(r0, r1, nv0) : row_max64<true>(r0, r1, nv0);
-          tmem_ld32(s_col + 64, r0);
-          tmem_ld32(s_col + 96, r1);
-          tmem_wait_ld();
-          mx = fmaxf(mx, whole1 ? row_max64<false>(r0, r1, nv1) : row_max64<true>(r0, r1, nv1));
-          m = mx * p.scale_log2;  // scale_log2 > 0 keeps the arg-max; -inf for empty rows
-          rs1 = exp_half(whole1, nv1);
-          if (!p_writable()) break;
-          tmem_st32(p_col + 32, pk);
-          tmem_ld32(s_col, r0);
-          tmem_ld32(s_col + 32, r1);
-          tmem_wait_ld();
-          s_done();
-          rs0 = exp_half(whole0, nv0);
+          m = fmaxf(v, pv);  // scale_log2 > 0 keeps the arg-max; -inf for empty rows
+          rs = exps();
         } else {
-          // Later tiles: one pass per half with the running reference m. exp2(x - m) is
-          // exact for any reference as long as x = S * scale - m stays small. A half's sum
-          // is at most 64 * 2^8 when every x <= 8 and above 2^8 when any x > 8 (or on
-          // overflow), so rows whose sum passes 2^8 recompute the true max and, where it
-          // passes the threshold, move m (O, l and P already stored are rescaled).
-          constexpr float kSumCheck = 256.f;
-          tmem_ld32(s_col + 64, r0);
-          tmem_ld32(s_col + 96, r1);
-          tmem_wait_ld();
-          rs1 = exp_half(whole1, nv1);
-          if (__any_sync(0xffffffffu, !(rs1 <= kSumCheck))) {
-            const float xm = xmax_half(whole1, nv1);
-            const bool mv = xm > kRescaleThreshold;
-            if (__any_sync(0xffffffffu, mv)) {
-              const float alpha = mv ? fast_exp2(-xm) : 1.f;
-              if (mv) m += xm;
-              if (!rescale_o(alpha)) break;
-              rs1 = exp_half(whole1, nv1);
-            }
-          }
-          if (!p_writable()) break;
-          tmem_st32(p_col + 32, pk);
-          tmem_ld32(s_col, r0);
-          tmem_ld32(s_col + 32, r1);
-          tmem_wait_ld();
-          s_done();
-          rs0 = exp_half(whole0, nv0);
-          if (__any_sync(0xffffffffu, !(rs0 <= kSumCheck))) {
-            const float xm = xmax_half(whole0, nv0);
-            const bool mv = xm > kRescaleThreshold;
-            if (__any_sync(0xffffffffu, mv)) {
-              const float alpha = mv ? fast_exp2(-xm) : 1.f;
-              if (mv) m += xm;
-              if (!rescale_o(alpha)) break;
-              rs1 *= alpha;
-              tmem_wait_st();
-              for (int c0 = 0; c0 < 32; c0 += 16) {
-                uint32_t pv[16];
-                tmem_ld16(p_col + 32 + c0, pv);
+          const float xm = fmaxf(v, pv);
+          const bool mv = xm > kRescaleThreshold;
+          if (__any_sync(0xffffffffu, mv)) {
+            // move m; O (my D/2 columns) and l follow once the previous PV has landed
+            const float alpha = mv ? fast_exp2(-xm) : 1.f;
+            if (mv) m += xm;
+            if (!mbar_wait_bounded(&o_done[h], (uint32_t)((n - 1) & 1), p.err)) step_ok = false;
+            step_ok = __all_sync(0xffffffffu, step_ok);
+            if (step_ok) {
+              tc_fence_after();
+              for (int c0 = 0; c0 < D / 2; c0 += 16) {
+                uint32_t o[16];
+                tmem_ld16(o_col + c0, o);
                 tmem_wait_ld();
 #pragma unroll
-                for (int c = 0; c < 16; ++c) pv[c] = scale_pair<T>(pv[c], alpha);
-                tmem_st16(p_col + 32 + c0, pv);
+                for (int c = 0; c < 16; ++c)
+                  o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+                tmem_st16(o_col + c0, o);
               }
-              rs0 = exp_half(whole0, nv0);
+              tmem_wait_st();
+              l *= alpha;
+              rs = exps();
             }
           }
         }
+        if constexpr (D == 64) {
+          // P has columns of its own: S may be overwritten by the next QK^T now, and P may
+          // be stored once the previous tile's PV has read the P before it
+          tc_fence_before();
+          mbar_arrive(&s_read[h]);
+          if (step_ok && n > 0 &&
+              !mbar_wait_bounded(&o_done[h], (uint32_t)((n - 1) & 1), p.err))
+            step_ok = false;
+          step_ok = __all_sync(0xffffffffu, step_ok);
+          if (step_ok) tc_fence_after();
+        }
+        if (!step_ok) {  // skip the rest of the tile; the next exchange tells the partner
+          ok = false;
+          continue;
+        }
         tmem_st32(p_col, pk);
-        l += rs1 + rs0;
+        l += rs;
         tmem_wait_st();
         // Keys past the context (the last KV tile's tail) may hold NaN/Inf in the pool;
         // P is 0 there but 0 * NaN is not: zero those V rows before the PV MMAs read them.
         // Head A's warps do it; head B's PV is issued after head A's.
-        const int tail0 = it.ctx - key0;  // first row of this tile past the context
+        const int tail0 = it.ctx - j * kN;  // first row of this tile past the context
         if (h == 0 && j == it.n_kv - 1 && tail0 < kN) {
           const int64_t gv = g;
           if (!mbar_wait_bounded(&v_full[gv & 1], (uint32_t)((gv >> 1) & 1), p.err)) ok = false;
           uint8_t* vt = smem + L::kOffV + (int)(gv & 1) * L::kKVBytes;
           const int zrows = kN - max(tail0, 0);
-          for (int e = threadIdx.x - 64; e < L::kChunks * zrows * 8; e += 128) {
+          for (int e = threadIdx.x - 64; e < L::kChunks * zrows * 8; e += 256) {
             const int c = e / (zrows * 8);         // d chunk
             const int rem = e - c * zrows * 8;
-            const int r = max(tail0, 0) + rem / 8;  // token row
-            const int q16 = rem % 8;                // 16-byte piece of the 128-byte line
-            reinterpret_cast<uint4*>(vt + c * (kN * 128) + r * 128)[q16] = make_uint4(0, 0, 0, 0);
+            const int rr = max(tail0, 0) + rem / 8;  // token row
+            const int q16 = rem % 8;                 // 16-byte piece of the 128-byte line
+            reinterpret_cast<uint4*>(vt + c * (kN * 128) + rr * 128)[q16] =
+                make_uint4(0, 0, 0, 0);
           }
           fence_proxy_async_smem();
         }
         tc_fence_before();
         mbar_arrive(&p_full[h]);
       }
-      // ---- epilogue: O / l -> out (the next item's first PV of this head waits for this
-      // warp's arrival on its first P, which comes after these reads)
-      if (ok) {
-        if (!mbar_wait_bounded(&o_done[h], (uint32_t)((n - 1) & 1), p.err)) ok = false;
-        ok = __all_sync(0xffffffffu, ok);
+      if (left) {
+        *abort_flag = 1;
+        break;
       }
-      if (ok) {
-        tc_fence_after();
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        // 32 columns at a time: each thread puts its row's 64 bytes in the warp's staging
-        // buffer (16-byte pieces XOR-swizzled by row), then the warp writes 8 rows x 64 B
-        // per store instruction instead of 32 scattered rows.
-        uint8_t* stage = smem + L::kOffStage + (warp - 2) * (32 * 64);
-        const int64_t row0 = (int64_t)it.q0 + it.qt * kM + quarter * 32;  // this warp's rows
-        const int nrows = min(32, it.rows_valid - quarter * 32);
-        T* obase = reinterpret_cast<T*>(p.out) + (int64_t)qh * p.o_head;
-        for (int c0 = 0; c0 < D; c0 += 32) {
-          uint32_t o[32];
-          tmem_ld32(o_col + c0, o);
-          tmem_wait_ld();
-          uint32_t pk[16];
+      // ---- epilogue: O / l -> out, each warp its D/2 columns (the next item's first PV of
+      // this head waits for this warp's arrival on its first P, which comes after these
+      // reads)
+      bool okw = ok;
+      if (okw && !mbar_wait_bounded(&o_done[h], (uint32_t)((n - 1) & 1), p.err)) okw = false;
+      okw = __all_sync(0xffffffffu, okw);
+      const float lp = exchange(l, okw, both);
+      if (!both) {
+        ok = false;
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const float lt = l + lp;
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      // 16 columns at a time: each thread puts its row's 32 bytes in the warp's staging
+      // buffer (16-byte pieces swapped on every fourth row), then the warp writes 16 rows x
+      // 32 B per store instruction
+      uint8_t* stage = smem + L::kOffStage + local * (32 * 32);
+      const int64_t row0 = (int64_t)it.q0 + it.qt * kM + quarter * 32;  // this warp's rows
+      const int nrows = min(32, it.rows_valid - quarter * 32);
+      T* obase = reinterpret_cast<T*>(p.out) + (int64_t)qh * p.o_head + (D / 2) * half;
+      const int sw = (lane >> 2) & 1;
+      for (int c0 = 0; c0 < D / 2; c0 += 16) {
+        uint32_t o[16];
+        tmem_ld16(o_col + c0, o);
+        tmem_wait_ld();
+        uint32_t pk8[8];
 #pragma unroll
-          for (int c = 0; c < 16; ++c)
-            pk[c] = pack2<T>(__uint_as_float(o[2 * c]) * inv, __uint_as_float(o[2 * c + 1]) * inv);
+        for (int c = 0; c < 8; ++c)
+          pk8[c] = pack2<T>(__uint_as_float(o[2 * c]) * inv, __uint_as_float(o[2 * c + 1]) * inv);
+        *reinterpret_cast<uint4*>(stage + lane * 32 + sw * 16) =
+            make_uint4(pk8[0], pk8[1], pk8[2], pk8[3]);
+        *reinterpret_cast<uint4*>(stage + lane * 32 + (sw ^ 1) * 16) =
+            make_uint4(pk8[4], pk8[5], pk8[6], pk8[7]);
+        __syncwarp();
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            *reinterpret_cast<uint4*>(stage + lane * 64 + ((c ^ ((lane >> 1) & 3)) * 16)) =
-                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-          __syncwarp();
-#pragma unroll
-          for (int pass = 0; pass < 4; ++pass) {
-            const int r = pass * 8 + (lane >> 2);
-            const int c = lane & 3;
-            if (r < nrows)
-              *reinterpret_cast<uint4*>(obase + (row0 + r) * p.o_tok + c0 + c * 8) =
-                  *reinterpret_cast<const uint4*>(stage + r * 64 + ((c ^ ((r >> 1) & 3)) * 16));
-          }
-          __syncwarp();
+        for (int pass = 0; pass < 2; ++pass) {
+          const int rr = pass * 16 + (lane >> 1);
+          const int c = lane & 1;
+          if (rr < nrows)
+            *reinterpret_cast<uint4*>(obase + (row0 + rr) * p.o_tok + c0 + c * 8) =
+                *reinterpret_cast<const uint4*>(stage + rr * 32 + ((c ^ ((rr >> 2) & 1)) * 16));
         }
-        tc_fence_before();
+        __syncwarp();
       }
-      if (!ok) *abort_flag = 1;
+      tc_fence_before();
     }
+    if (!ok) *abort_flag = 1;
   }
 
   // ---- teardown: every TMA and MMA of this CTA has finished before TMEM is freed
