@@ -73,11 +73,11 @@ sys.path.insert(0, str(REPO))
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of K2 on the
 # decode workload (append mode: the KV write fused in), from one ncu capture of a K2 launch
-# over the same sequences and block tables: 616.68 MB read + 7.28 MB written.
-K2_TRAFFIC_BYTES: float | None = 623.967232e6
+# over the same sequences and block tables: 616.26 MB read + 6.43 MB written.
+K2_TRAFFIC_BYTES: float | None = 622.695936e6
 # The same for K3 on the 32-prompt prefill workload, from one ncu capture of a K3 launch:
-# 211.81 MB read + 117.18 MB written.
-K3_TRAFFIC_BYTES: float | None = 328.994816e6
+# 212.31 MB read + 116.40 MB written.
+K3_TRAFFIC_BYTES: float | None = 328.702464e6
 # The same for K2 on the long-context workload, from a capture over a one-layer pool with
 # the same sequences and tables (per-launch traffic does not depend on the pool's layer
 # count): 2,599.38 MB read + 9.10 MB written.
