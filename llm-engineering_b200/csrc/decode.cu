@@ -263,6 +263,13 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
+  // Programmatic dependent launch: this grid may be scheduled while the previous kernel on
+  // the stream is finishing. It reads and writes no global memory before that kernel has
+  // completed and its writes are visible (the wait), and it lets the next launch on the
+  // stream get scheduled the same way (the trigger). Only the launch and scheduling of the
+  // CTAs overlap; with a predecessor that never triggers, the wait returns at once.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   // Warps w and w+1 (2 KV heads) or w..w+3 (4 heads) stream the same sub-blocks for
@@ -1074,10 +1081,18 @@ int decode_impl(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
   p.vpool = static_cast<uint8_t*>(const_cast<void*>(value_cache));
   p.num_kv_heads = num_kv_heads;
 
-  dim3 grid((unsigned)ctas, (unsigned)(num_kv_heads / hpu));
   void* args[] = {&kmap, &vmap, &p};
-  cudaError_t e = cudaLaunchKernel(pl.fn, grid, dim3(pl.warps * 32), args, (size_t)pl.smem,
-                                   static_cast<cudaStream_t>(stream));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)ctas, (unsigned)(num_kv_heads / hpu));
+  cfg.blockDim = dim3(pl.warps * 32);
+  cfg.dynamicSmemBytes = (size_t)pl.smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelExC(&cfg, pl.fn, args);
   if (e != cudaSuccess) return b2p_host::record_error(e);
   return b2p_host::check_launch();
 }
