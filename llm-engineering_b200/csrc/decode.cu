@@ -671,7 +671,10 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
   __syncwarp();
   int last_mask = 0;
   if (lane == 0) {
-    __threadfence();  // the partials are visible before the counts say so
+    // Release: the partial records written above (by every lane, ordered before this by
+    // __syncwarp) are visible before the counts say so. fence.acq_rel with relaxed atomics
+    // is the release/acquire pattern of the PTX memory model, lighter than a full fence.
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
     int prev[2] = {0, 0};
     for (int j = 0; j < npend; ++j)  // both atomics in flight together
       prev[j] = atomicAdd(p.counters + (size_t)head * p.num_seqs + pend_seq[j], 1);
@@ -683,7 +686,8 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
         last_mask |= 1 << j;
       }
     }
-    if (last_mask) __threadfence();
+    // acquire: a last contributor reads the others' records after their counts
+    if (last_mask) asm volatile("fence.acq_rel.gpu;" ::: "memory");
   }
   last_mask = __shfl_sync(0xffffffffu, last_mask, 0);
   for (int j = 0; j < npend; ++j) {
