@@ -1292,6 +1292,87 @@ def _public(d: dict) -> dict:
     return {k: v for k, v in d.items() if not k.startswith("_")}
 
 
+LM_ROWS, LM_HIDDEN, LM_VOCAB = 192, 1536, 151936
+
+
+def lm_head_section(run: Run, ops, args) -> dict:
+    """K6 — the LM head fused with the greedy argmax — on a decode step's rows: 192 last
+    hidden states (hidden 1536) against the Qwen2.5-1.5B LM head (151936 x 1536 bf16, 467 MB,
+    larger than L2, so every launch streams it from HBM). Beside it, the unfused path the
+    engine takes otherwise: cuBLAS logits (192 x 151936, bf16) and torch's argmax."""
+    dev, stream = run.dev, run.stream
+    g = torch.Generator(device=dev).manual_seed(606)
+    hidden = (torch.randn(LM_ROWS, LM_HIDDEN, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    weight = (torch.randn(LM_VOCAB, LM_HIDDEN, device=dev, generator=g)
+              / LM_HIDDEN ** 0.5).to(torch.bfloat16)
+    ws = torch.zeros(ops.lm_head_argmax_workspace_size(LM_ROWS), dtype=torch.uint8, device=dev)
+    ids = torch.empty(LM_ROWS, dtype=torch.int64, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def fused():
+        ops.lm_head_argmax(hidden, weight, ws, out_ids=ids, err_flag=err)
+
+    def unfused():
+        return torch.argmax(hidden @ weight.T, dim=-1)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        run.barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        run.barrier()
+        return run.max(t0.elapsed_time(t1) / args.steps)[0]
+
+    with ClockSampler(dev) as clocks:
+        k6_ms = timed(fused)
+    torch_ms = timed(unfused)
+    if int(err.item()) != 0:
+        raise RuntimeError(f"device error flag set: {int(err.item())}")
+    same = bool(torch.equal(ids, unfused()))
+    # e2e through the public API: hidden states from pinned host memory in, ids out
+    h_hidden = hidden.cpu().pin_memory()
+    h_ids = torch.empty(LM_ROWS, dtype=torch.int64).pin_memory()
+    d_hidden = torch.empty_like(hidden)
+
+    def e2e():
+        d_hidden.copy_(h_hidden, non_blocking=True)
+        ops.lm_head_argmax(d_hidden, weight, ws, out_ids=ids, err_flag=err)
+        h_ids.copy_(ids, non_blocking=True)
+    e2e_ms = timed(e2e)
+    algo = LM_VOCAB * LM_HIDDEN * 2 + LM_ROWS * LM_HIDDEN * 2 + LM_ROWS * 8
+    flops = 2.0 * LM_ROWS * LM_VOCAB * LM_HIDDEN
+    peaks = _peaks()
+    us = k6_ms * 1e3
+    gbs = algo / (us * 1e-6) / 1e9
+    world = run.world
+    return {
+        "metric": "greedy rows/s (LM head fused with argmax, Qwen2.5-1.5B head, bf16)",
+        "value": round(world * LM_ROWS / (k6_ms * 1e-3), 1), "unit": "rows/s",
+        "steps": args.steps, "ms_per_step": round(k6_ms, 4), "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) hidden states, N(0,1/1536) head weights)",
+        "config": {"workload": f"{LM_ROWS} rows x hidden {LM_HIDDEN} against a {LM_VOCAB} x "
+                               f"{LM_HIDDEN} LM head", "l2": "head larger than L2 (467 MB)"},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm"],
+                     "unit": "GB/s", "frac": round(gbs / peaks["hbm"], 4),
+                     "peak_source": f"{peaks['source']} hbm_gbs", "algorithmic_bytes": algo,
+                     "tflops": round(flops / (us * 1e-6) / 1e12, 1),
+                     "tensor_frac": round(flops / (us * 1e-6) / 1e12 / peaks["bf16"], 4),
+                     "kernel": "lm_head_argmax_tc", "kernel_us": round(us, 2)},
+        "unfused_torch_us": round(torch_ms * 1e3, 2),
+        "speedup_vs_unfused": round(torch_ms / k6_ms, 3),
+        "ids_equal_unfused": same,
+        "e2e": {"value": round(world * LM_ROWS / (e2e_ms * 1e-3), 1), "unit": "rows/s",
+                "h2d_bytes_per_step": h_hidden.numel() * 2, "d2h_bytes_per_step": LM_ROWS * 8},
+        "gpu_launches": 2 * (args.steps + args.warmup) + args.warmup + args.steps,
+        "clocks": clocks.summary(),
+    }
+
+
 def run_default(args) -> None:
     """The headline decode line with the prefill, long-context and engine sub-objects."""
     ops = _load_ops()
@@ -1313,6 +1394,9 @@ def run_default(args) -> None:
                                       + line["longctx"]["gpu_launches"]
                                       + line["model"]["gpu_launches"])
         line["c1"] = c1_section(run, args)
+        torch.cuda.empty_cache()
+        line["lm_head"] = lm_head_section(run, ops, args)
+        line["gpu_launches_total"] += line["lm_head"]["gpu_launches"]
         torch.cuda.empty_cache()
     if run.rank == 0:
         if run.world == 1 and not args.no_cpu_baseline:
@@ -1372,6 +1456,15 @@ def run_mixed(args) -> None:
     line["offered_load"] = offered_load(run, engine, RequestStream(1000, run.rank, run.world),
                                         args.duration)
     run.barrier()
+    if run.rank == 0:
+        print(json.dumps(line), flush=True)
+    run.close()
+
+
+def run_lmhead(args) -> None:
+    ops = _load_ops()
+    run = Run()
+    line = _headline(lm_head_section(run, ops, args), run, args)
     if run.rank == 0:
         print(json.dumps(line), flush=True)
     run.close()
@@ -1470,11 +1563,13 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["decode", "prefill", "longctx", "mixed", "metadata"],
+    ap.add_argument("--workload", choices=["decode", "prefill", "longctx", "mixed", "metadata",
+                                           "lmhead"],
                     default="decode",
                     help="decode (default): the headline decode line with the prefill, "
                          "long-context and engine sub-objects; prefill / longctx / mixed: that "
-                         "configuration as its own line; metadata: K4 on a mixed step")
+                         "configuration as its own line; metadata: K4 on a mixed step; "
+                         "lmhead: K6 (LM head + greedy argmax) as its own line")
     ap.add_argument("--layers", type=int, default=NUM_LAYERS,
                     help="layers of the decode pool (28 for the metric; fewer for profiling)")
     ap.add_argument("--longctx-layers", type=int, default=NUM_LAYERS,
@@ -1500,6 +1595,8 @@ def main() -> None:
         run_longctx(args)
     elif args.workload == "mixed":
         run_mixed(args)
+    elif args.workload == "lmhead":
+        run_lmhead(args)
     elif args.workload == "metadata":
         run_metadata(args)
     else:

@@ -256,6 +256,29 @@ B2P_API int b2p_build_metadata(const int32_t* query_lens, const int32_t* context
                        int max_blocks_per_seq, int64_t total_q, int32_t* err_flag,
                        void* stream);
 
+/* K6 — LM head fused with the greedy argmax. Replaces, for greedy rows, the LM head over
+ * each execution's last row plus the argmax over its logits
+ * (serving/engine/paged_model_runner.py:83-91, serving/engine/sampling.py:78-79):
+ *   out_ids[r] = argmax_v round(hidden[r] . weight[v])   for r < rows
+ * where round() is the rounding to the model dtype (the reference's LM head returns bf16 /
+ * f16 logits and takes the argmax of those; equal values go to the lowest index, as torch's
+ * argmax does). The (rows, vocab) logits are never written. hidden [rows, hidden_size] and
+ * weight [vocab, hidden_size] are bf16 or f16 (dtype B2P_BF16 / B2P_F16), row-major with the
+ * given row strides (elements), 16-byte aligned; hidden_size a multiple of 64.
+ * out_max (optional, nullable) receives the rounded maximum logit of each row.
+ * workspace: b2p_lm_head_argmax_workspace_size(rows) bytes, 8-byte aligned and zero before
+ * the first launch; every launch that runs to its end leaves it zero again.
+ * Returns B2P_EUNSUPPORTED for other dtypes or shapes (the caller keeps its logits path),
+ * B2P_EWORKSPACE when the workspace is too small (nothing queued). No reference function
+ * has this form: it fuses two reference steps.
+ */
+B2P_API size_t b2p_lm_head_argmax_workspace_size(int rows);
+B2P_API int b2p_lm_head_argmax(const void* hidden, int64_t hidden_row_stride, const void* weight,
+                               int64_t weight_row_stride, int rows, int64_t vocab,
+                               int hidden_size, int dtype, int64_t* out_ids, float* out_max,
+                               void* workspace, size_t workspace_bytes, int32_t* err_flag,
+                               void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -42,6 +42,8 @@ EXPORTED_SYMBOLS = (
     "b2p_paged_decode_append",
     "b2p_paged_prefill",
     "b2p_build_metadata",
+    "b2p_lm_head_argmax_workspace_size",
+    "b2p_lm_head_argmax",
 )
 
 _lock = threading.Lock()
@@ -88,6 +90,11 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "b2p_build_metadata": (
         _i32,
         [_p, _p, _p, _i32, _p, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _i32, _i64, _p, _p],
+    ),
+    "b2p_lm_head_argmax_workspace_size": (_sz, [_i32]),
+    "b2p_lm_head_argmax": (
+        _i32,
+        [_p, _i64, _p, _i64, _i32, _i64, _i32, _i32, _p, _p, _p, _sz, _p, _p],
     ),
 }
 

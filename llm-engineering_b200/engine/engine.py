@@ -78,7 +78,13 @@ class Engine:
                        for s, c in zip(out.prefill_sequences, chunks, strict=True)]
         if not executions:
             return ()
-        logits = self.model_runner.forward(executions)
+        # Every row greedy: a runner that has it picks the ids with the LM head fused into
+        # the argmax (no logits); otherwise logits, then the samplers.
+        fused = None
+        if all(ex.sequence.request.sampling_parameters.greedy for ex in executions):
+            pick = getattr(self.model_runner, "greedy_tokens", None)
+            fused = pick(executions) if pick is not None else None
+        logits = self.model_runner.forward(executions) if fused is None else None
         # A chunk that leaves part of its history for later steps yields no token.
         partial = set()
         if out.prefill_chunks:
@@ -90,7 +96,10 @@ class Engine:
         greedy_rows = [i for i, ex in enumerate(executions)
                        if i not in partial and ex.sequence.request.sampling_parameters.greedy]
         greedy: dict[int, int] = {}
-        if greedy_rows:
+        if fused is not None:
+            ids = fused.tolist()
+            greedy = {i: ids[i] for i in greedy_rows}
+        elif greedy_rows:
             picks = Sampler.greedy_batch(logits[greedy_rows] if len(greedy_rows) != len(executions)
                                          else logits)
             greedy = dict(zip(greedy_rows, picks, strict=True))

@@ -302,3 +302,55 @@ def build_metadata(
     )
     _lib.check(rc, "b2p_build_metadata")
     return out
+
+
+def lm_head_argmax_workspace_size(rows: int) -> int:
+    """Bytes of the K6 workspace for up to ``rows`` rows (keys and a counter)."""
+    return int(_lib.load().b2p_lm_head_argmax_workspace_size(rows))
+
+
+def lm_head_argmax(
+    hidden: torch.Tensor,
+    weight: torch.Tensor,
+    workspace: torch.Tensor,
+    out_ids: torch.Tensor | None = None,
+    out_max: torch.Tensor | None = None,
+    err_flag: torch.Tensor | None = None,
+) -> torch.Tensor | None:
+    """K6: greedy token ids ``argmax_v round(hidden[r] . weight[v])`` for every row of hidden.
+
+    hidden (rows, hidden_size) and weight (vocab, hidden_size) are bf16 or f16 CUDA tensors
+    with contiguous rows; the logits are rounded to their dtype before the argmax (the LM
+    head's own output type) and never written. ``workspace`` is a uint8 CUDA tensor of at
+    least ``lm_head_argmax_workspace_size(rows)`` bytes, zero before its first use (each
+    launch leaves it zero). Returns the int64 ids, or None when the dtype or shape is
+    outside what the kernel takes (the caller then computes logits).
+    """
+    _require_cuda("hidden", hidden)
+    _require_cuda("weight", weight)
+    _require_cuda("workspace", workspace)
+    if hidden.dim() != 2 or weight.dim() != 2 or hidden.shape[1] != weight.shape[1]:
+        raise ValueError("hidden must be (rows, hidden_size) and weight (vocab, hidden_size)")
+    if hidden.dtype != weight.dtype:
+        raise ValueError("hidden and weight dtypes differ")
+    if hidden.stride(1) != 1 or weight.stride(1) != 1:
+        raise ValueError("hidden and weight rows must be contiguous")
+    rows, size = hidden.shape
+    if hidden.dtype not in (torch.bfloat16, torch.float16):
+        return None
+    dev = hidden.device
+    if out_ids is None:
+        out_ids = torch.empty(rows, dtype=torch.int64, device=dev)
+    if out_ids.dtype != torch.int64 or out_ids.numel() < rows or not out_ids.is_contiguous():
+        raise ValueError("out_ids must be a contiguous int64 tensor of at least rows entries")
+    if out_max is not None and (out_max.dtype != torch.float32 or out_max.numel() < rows):
+        raise ValueError("out_max must be a float32 tensor of at least rows entries")
+    rc = _lib.load().b2p_lm_head_argmax(
+        hidden.data_ptr(), hidden.stride(0), weight.data_ptr(), weight.stride(0), rows,
+        weight.shape[0], size, dtype_code(hidden.dtype), out_ids.data_ptr(), _ptr(out_max),
+        workspace.data_ptr(), workspace.numel(), _ptr(err_flag), _stream(dev),
+    )
+    if rc == _lib.B2P_EUNSUPPORTED:
+        return None
+    _lib.check(rc, "b2p_lm_head_argmax")
+    return out_ids[:rows]

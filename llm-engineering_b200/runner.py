@@ -22,6 +22,10 @@ Here the same ``ModelRunner.forward(executions) -> (B, vocab)`` interface
     building any mask.
   * ``logits_to_keep`` restricts the LM head to each execution's last query row, which is
     exactly the rows the reference keeps with ``index_select`` (paged_model_runner.py:85-91).
+  * ``greedy_tokens`` (an addition to the interface, used by this package's engine when
+    every row of a step is greedy): K6 (``ops.lm_head_argmax``) computes the LM head over
+    those rows and keeps only each row's arg-max, in place of ``forward`` + ``argmax``
+    (serving/engine/sampling.py:78-79).
 
 Executions may come from the reference engine (``slot_ids`` over the whole history) or
 from this package's engine (``block_ids``). Slot ids that follow the block structure
@@ -272,6 +276,7 @@ class B200PagedModelRunner:
         self._workspace = torch.zeros(16, dtype=torch.uint8, device=self._device)
         self._err = torch.zeros(1, dtype=torch.int32, device=self._device)
         self._mirror: _TableMirror | None = None
+        self._k6_workspace: torch.Tensor | None = None
 
     # ------------------------------------------------------------------ host metadata
     @staticmethod
@@ -396,6 +401,52 @@ class B200PagedModelRunner:
     # ------------------------------------------------------------------ ModelRunner
     def forward(self, executions: Sequence) -> torch.Tensor:
         """Next-token logits (B, vocab) for the executions, in their order."""
+        out = self._run(executions, lambda batch, input_ids, cache: self._model(
+            input_ids=input_ids.unsqueeze(0), position_ids=batch.positions.unsqueeze(0),
+            attention_mask=None, past_key_values=cache, use_cache=True,
+            logits_to_keep=batch.logit_indices))
+        return out.logits[0]
+
+    def greedy_tokens(self, executions: Sequence) -> torch.Tensor | None:
+        """Greedy next-token ids (B,) int64 on the device, in the executions' order.
+
+        The same forward as ``forward`` up to the final norm, then K6 (the LM head fused with
+        the argmax, ``ops.lm_head_argmax``) on each execution's last row: the ids equal the
+        argmax of the logits ``forward`` returns (the rounding to the model dtype included),
+        and the (B, vocab) logits are never written. Returns None, without running
+        anything, when the model has no plain bias-free LM head over a ``model`` body or its
+        dtype / hidden size is outside what K6 takes (the caller then uses ``forward``).
+        """
+        head = self._lm_head()
+        if head is None:
+            return None
+        n = len(executions)
+        if self._k6_workspace is None or self._k6_workspace.numel() < _ops.lm_head_argmax_workspace_size(n):
+            self._k6_workspace = torch.zeros(_ops.lm_head_argmax_workspace_size(max(n, 256)),
+                                             dtype=torch.uint8, device=self._device)
+        def run(batch, input_ids, cache):
+            out = self._model.model(input_ids=input_ids.unsqueeze(0),
+                                    position_ids=batch.positions.unsqueeze(0), attention_mask=None,
+                                    past_key_values=cache, use_cache=True)
+            hidden = out.last_hidden_state[0].index_select(0, batch.logit_indices)
+            return _ops.lm_head_argmax(hidden, head, self._k6_workspace, err_flag=self._err)
+        return self._run(executions, run)
+
+    def _lm_head(self) -> torch.Tensor | None:
+        """The LM head weight when K6 can stand in for it (else None)."""
+        lm = getattr(self._model, "lm_head", None)
+        body = getattr(self._model, "model", None)
+        if not isinstance(lm, torch.nn.Linear) or lm.bias is not None or body is None:
+            return None
+        w = lm.weight
+        if (w.dtype not in (torch.bfloat16, torch.float16) or not w.is_cuda
+                or w.shape[1] % 64 != 0 or w.stride(1) != 1
+                or getattr(self._model.config, "final_logit_softcapping", None)):
+            return None
+        return w
+
+    def _run(self, executions: Sequence, fn):
+        """One packed step: batch metadata, the model call ``fn``, the device-error check."""
         if not executions:
             raise ValueError("At least one execution is required.")
         fallbacks = self._fallbacks()
@@ -404,10 +455,7 @@ class B200PagedModelRunner:
         token = _active_batch.set(batch)
         try:
             with torch.inference_mode():
-                out = self._model(input_ids=input_ids.unsqueeze(0),
-                                  position_ids=batch.positions.unsqueeze(0), attention_mask=None,
-                                  past_key_values=cache, use_cache=True,
-                                  logits_to_keep=batch.logit_indices)
+                out = fn(batch, input_ids, cache)
         finally:
             _active_batch.reset(token)
         bits = self.device_error()
@@ -420,8 +468,8 @@ class B200PagedModelRunner:
             warnings.warn(
                 f"{self._storage.key_cache.dtype} paged attention ran on the CUDA-core kernels "
                 "(block size, head_dim, GQA group or row alignment outside what the tensor-core "
-                "kernels take); expect a large slowdown", RuntimeWarning, stacklevel=2)
-        return out.logits[0]
+                "kernels take); expect a large slowdown", RuntimeWarning, stacklevel=3)
+        return out
 
     @staticmethod
     def _fallbacks() -> tuple[int, int] | None:

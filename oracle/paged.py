@@ -231,3 +231,16 @@ def prefill_attention(q: torch.Tensor, key_cache: torch.Tensor, value_cache: tor
         k, v = gather(key_cache, value_cache, layer, slots.tolist())
         out.append(_attend(q[a:b].float(), k.float(), v.float(), scale, ctx - (b - a)))
     return torch.cat(out, dim=0)
+
+
+# --------------------------------------------------------------------- greedy sampling
+def greedy_tokens(hidden: torch.Tensor, weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """The reference's greedy pick for each row: the LM head over the row's last hidden
+    state (``lm_head`` + ``index_select`` of the logit rows,
+    serving/engine/paged_model_runner.py:83-91), whose logits come out in the model dtype,
+    then ``argmax`` (serving/engine/sampling.py:78-79; torch returns the first of equal
+    maxima). Computed on the CPU in fp32, rounded to the weight dtype. Returns (ids, max)."""
+    logits = (hidden.float().cpu() @ weight.float().cpu().T).to(weight.dtype).float()
+    best = logits.max(-1).values
+    ids = torch.argmax(logits, -1)
+    return ids, best
