@@ -1302,15 +1302,20 @@ def lm_head_section(run: Run, ops, args) -> dict:
     engine takes otherwise: cuBLAS logits (192 x 151936, bf16) and torch's argmax."""
     dev, stream = run.dev, run.stream
     g = torch.Generator(device=dev).manual_seed(606)
-    hidden = (torch.randn(LM_ROWS, LM_HIDDEN, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    # the runner's layout: the step's rows in a buffer padded to K6's 128-row tiles
+    padded = LM_ROWS + (-LM_ROWS) % 128
+    buf = torch.zeros(padded, LM_HIDDEN, dtype=torch.bfloat16, device=dev)
+    buf[:LM_ROWS] = (torch.randn(LM_ROWS, LM_HIDDEN, device=dev, generator=g) * 0.5)
+    hidden = buf[:LM_ROWS]
     weight = (torch.randn(LM_VOCAB, LM_HIDDEN, device=dev, generator=g)
               / LM_HIDDEN ** 0.5).to(torch.bfloat16)
-    ws = torch.zeros(ops.lm_head_argmax_workspace_size(LM_ROWS), dtype=torch.uint8, device=dev)
-    ids = torch.empty(LM_ROWS, dtype=torch.int64, device=dev)
+    ws = torch.zeros(ops.lm_head_argmax_workspace_size(padded), dtype=torch.uint8, device=dev)
+    ids_buf = torch.empty(padded, dtype=torch.int64, device=dev)
+    ids = ids_buf[:LM_ROWS]
     err = torch.zeros(1, dtype=torch.int32, device=dev)
 
     def fused():
-        ops.lm_head_argmax(hidden, weight, ws, out_ids=ids, err_flag=err)
+        ops.lm_head_argmax(buf, weight, ws, out_ids=ids_buf, err_flag=err, rows=LM_ROWS)
 
     def unfused():
         return torch.argmax(hidden @ weight.T, dim=-1)
@@ -1337,11 +1342,10 @@ def lm_head_section(run: Run, ops, args) -> dict:
     # e2e through the public API: hidden states from pinned host memory in, ids out
     h_hidden = hidden.cpu().pin_memory()
     h_ids = torch.empty(LM_ROWS, dtype=torch.int64).pin_memory()
-    d_hidden = torch.empty_like(hidden)
 
     def e2e():
-        d_hidden.copy_(h_hidden, non_blocking=True)
-        ops.lm_head_argmax(d_hidden, weight, ws, out_ids=ids, err_flag=err)
+        hidden.copy_(h_hidden, non_blocking=True)
+        ops.lm_head_argmax(buf, weight, ws, out_ids=ids_buf, err_flag=err, rows=LM_ROWS)
         h_ids.copy_(ids, non_blocking=True)
     e2e_ms = timed(e2e)
     algo = LM_VOCAB * LM_HIDDEN * 2 + LM_ROWS * LM_HIDDEN * 2 + LM_ROWS * 8

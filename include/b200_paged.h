@@ -264,7 +264,8 @@ B2P_API int b2p_build_metadata(const int32_t* query_lens, const int32_t* context
  * f16 logits and takes the argmax of those; equal values go to the lowest index, as torch's
  * argmax does). The (rows, vocab) logits are never written. hidden [rows, hidden_size] and
  * weight [vocab, hidden_size] are bf16 or f16 (dtype B2P_BF16 / B2P_F16), row-major with the
- * given row strides (elements), 16-byte aligned; hidden_size a multiple of 64.
+ * given row strides (elements), 16-byte aligned; hidden_size a multiple of 64 and rows a
+ * multiple of 128 (pad the hidden rows; the ids of padding rows are computed and unused).
  * out_max (optional, nullable) receives the rounded maximum logit of each row.
  * workspace: b2p_lm_head_argmax_workspace_size(rows) bytes, 8-byte aligned and zero before
  * the first launch; every launch that runs to its end leaves it zero again.

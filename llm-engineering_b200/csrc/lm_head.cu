@@ -8,22 +8,26 @@
 // index, so the (B, 151936) logits never reach HBM:
 //
 //   logits tile = H (smem, K-major: rows x hidden) x W^T (smem, K-major: vocab x hidden),
-//                 tcgen05.mma kind::f16, M = 128 rows, N = 128 vocab entries, fp32 in TMEM
+//                 tcgen05.mma kind::f16, M = 128 rows, N = 256 vocab entries, fp32 in TMEM
 //   per row: max and first arg-max over the tile, each logit rounded to the model dtype
 //            first (the reference's LM head returns bf16/f16 logits and takes argmax of
 //            those, ties to the lowest index)
 //
-// Work item = (group of up to 256 rows, 128-entry vocab tile); the two 128-row halves of a
-// group share each W tile (one W read per group). Persistent CTAs walk the items round
+// Work item = (group of up to 256 rows, 256-entry vocab tile); the two 128-row halves of a
+// group share each W tile (one W read per group), and each hidden chunk serves 256 vocab
+// entries (N = 256 MMAs: half the instructions and hidden re-reads of N = 128 ones, which
+// measured 1.4x slower). Persistent CTAs walk the items round
 // robin; each keeps a running best per row while its items stay in one row group and
 // merges it into a per-row 64-bit key with atomicMax (value in the high word, ordered so
 // that larger logits give larger keys; ~index in the low word, so equal values keep the
 // lowest index). The last CTA to finish turns the keys into token ids and re-zeroes them.
 //
 // Warp roles (192 threads): warp 0 = TMA producer (hidden and W chunks of 64 elements,
-// 128-byte swizzle, 4 stages), warp 1 = tensor-memory owner and MMA issuer, warps 2..5 =
-// epilogue (one TMEM lane quarter each). TMEM holds two accumulator buffers of two 128-row
-// halves (4 x 128 columns), so the epilogue of one item overlaps the MMAs of the next.
+// 128-byte swizzle, 3 stages of 64 KB), warp 1 = tensor-memory owner and MMA issuer, warps
+// 2..5 = epilogue (one TMEM lane quarter each). TMEM holds the accumulators of both 128-row
+// halves (2 x 256 columns); the next item's first MMA waits for the epilogue's reads.
+// Hidden rows are padded by the caller to a multiple of 128, so no box reaches past them
+// (boxes that do are filled row by row and measured 1.6x slower for a single row).
 #include <type_traits>
 
 #include "common.cuh"
@@ -34,9 +38,9 @@ namespace {
 using namespace b2p;
 
 constexpr int kRowsTile = 128;   // rows per MMA (TMEM lanes)
-constexpr int kVocabTile = 128;  // vocab entries per MMA (N)
+constexpr int kVocabTile = 256;  // vocab entries per MMA (N)
 constexpr int kGroupRows = 2 * kRowsTile;
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr int kThreads = 192;
 constexpr int kEpilogueWarps = 4;
 constexpr uint32_t kTmemCols = 512;
@@ -47,7 +51,7 @@ struct LmHeadParams {
   int64_t vocab;
   int hidden;            // multiple of 64
   int n_groups;          // ceil(rows / 256)
-  int64_t n_vtiles;      // ceil(vocab / 128)
+  int64_t n_vtiles;      // ceil(vocab / 256)
   unsigned long long* keys;  // [rows], zero between launches
   int32_t* ctr;          // CTAs done, zero between launches
   int64_t* out_ids;      // [rows]
@@ -55,11 +59,12 @@ struct LmHeadParams {
   int32_t* err;
 };
 
-// Shared-memory plan: per stage the two row halves' hidden chunks and the W chunk.
+// Shared-memory plan: per stage the two row halves' hidden chunks and the W chunk (256 rows).
 struct Plan {
-  static constexpr int kStageBytes = 3 * kChunkBytes;
+  static constexpr int kWBytes = kVocabTile * 128;
+  static constexpr int kStageBytes = 2 * kChunkBytes + kWBytes;
   static constexpr int kOffBar = kStages * kStageBytes;
-  // full[4], empty[4], acc_full[2], acc_empty[2]
+  // full[3], empty[3], acc_full[2], acc_empty[2] (one accumulator: index 0 only)
   static constexpr int kNumBars = 2 * kStages + 4;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffMisc + 16;
@@ -147,7 +152,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           uint8_t* st = smem + s * Plan::kStageBytes;
-          mbar_arrive_expect_tx(&full[s], (uint32_t)((halves + 1) * kChunkBytes));
+          mbar_arrive_expect_tx(&full[s], (uint32_t)(halves * kChunkBytes + Plan::kWBytes));
           for (int h = 0; h < halves; ++h)
             tma_load_4d(st + h * kChunkBytes, &hmap, &full[s], 0, kc, 0, row0 + h * kRowsTile);
           tma_load_4d(st + 2 * kChunkBytes, &wmap, &full[s], 0, kc, 0, (int)(vt * kVocabTile));
@@ -165,14 +170,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc = idesc_f16(ab, kRowsTile, kVocabTile, 0, 0);
       const uint64_t d0 = smem_desc_sw128(smem_u32(smem), 16, 1024);
       int64_t q = 0;
-      int li = 0;  // items of this CTA (accumulator buffer = li & 1)
+      int li = 0;  // items of this CTA (accumulator phases)
       bool ok = true;
       for (int64_t it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++li) {
         const int grp = (int)(it / p.n_vtiles);
         const int halves = p.rows - grp * kGroupRows > kRowsTile ? 2 : 1;
-        const int b = li & 1;
-        // buffer b is free once the epilogue has read item li - 2
-        if (li >= 2 && !mbar_wait_bounded(&acc_empty[b], (uint32_t)(((li >> 1) - 1) & 1), p.err)) {
+        // the accumulator is free once the epilogue has read item li - 1
+        if (li >= 1 && !mbar_wait_bounded(&acc_empty[0], (uint32_t)((li - 1) & 1), p.err)) {
           ok = false;
           break;
         }
@@ -189,14 +193,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t bw = stage + (uint64_t)((2 * kChunkBytes + kk * 32) >> 4);
             for (int h = 0; h < halves; ++h)
-              mma_ss(tbase + 256u * b + 128u * h,
+              mma_ss(tbase + 256u * h,
                      stage + (uint64_t)((h * kChunkBytes + kk * 32) >> 4), bw, idesc,
                      (kc > 0 || kk > 0) ? 1u : 0u);
           }
           mma_commit(&empty[s]);
         }
         if (!ok) break;
-        mma_commit(&acc_full[b]);
+        mma_commit(&acc_full[0]);
       }
       if (!ok) *abort_flag = 1;
     }
@@ -228,8 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int grp = (int)(it / p.n_vtiles);
       const int64_t vt = it % p.n_vtiles;
       const int halves = p.rows - grp * kGroupRows > kRowsTile ? 2 : 1;
-      const int b = li & 1;
-      bool ok = !*abort_flag && mbar_wait_bounded(&acc_full[b], (uint32_t)((li >> 1) & 1), p.err);
+      bool ok = !*abort_flag && mbar_wait_bounded(&acc_full[0], (uint32_t)(li & 1), p.err);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) {
         *abort_flag = 1;
@@ -245,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
         for (int c0 = 0; c0 < kVocabTile; c0 += 32) {
           uint32_t v[32];
-          tmem_ld32(lane_base + 256u * b + 128u * h + c0, v);
+          tmem_ld32(lane_base + 256u * h + c0, v);
           tmem_wait_ld();
           // columns past the vocabulary hold the zero-filled W rows' products: skip them
           const int64_t left = p.vocab - (col0 + c0);
@@ -263,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&acc_empty[b]);
+      mbar_arrive(&acc_empty[0]);
     }
     flush();
   }
@@ -318,7 +321,7 @@ int b2p_lm_head_argmax(const void* hidden, int64_t hidden_row_stride,
     return B2P_EINVAL;
   if (rows == 0) return B2P_OK;
   if ((dtype != B2P_BF16 && dtype != B2P_F16) || hidden_size % 64 != 0 ||
-      vocab > 0x7fffffffLL - kVocabTile)
+      vocab > 0x7fffffffLL - kVocabTile || rows % kRowsTile != 0)
     return B2P_EUNSUPPORTED;
   auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
   if (!al16(hidden) || !al16(weight) || (hidden_row_stride * 2) % 16 ||

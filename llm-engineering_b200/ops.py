@@ -305,8 +305,9 @@ def build_metadata(
 
 
 def lm_head_argmax_workspace_size(rows: int) -> int:
-    """Bytes of the K6 workspace for up to ``rows`` rows (keys and a counter)."""
-    return int(_lib.load().b2p_lm_head_argmax_workspace_size(rows))
+    """Bytes of the K6 workspace for up to ``rows`` rows (keys and a counter; rows are
+    counted rounded up to the kernel's 128-row tiles)."""
+    return int(_lib.load().b2p_lm_head_argmax_workspace_size(rows + (-rows) % 128))
 
 
 def lm_head_argmax(
@@ -316,15 +317,20 @@ def lm_head_argmax(
     out_ids: torch.Tensor | None = None,
     out_max: torch.Tensor | None = None,
     err_flag: torch.Tensor | None = None,
+    rows: int | None = None,
 ) -> torch.Tensor | None:
-    """K6: greedy token ids ``argmax_v round(hidden[r] . weight[v])`` for every row of hidden.
+    """K6: greedy token ids ``argmax_v round(hidden[r] . weight[v])`` for the first ``rows``
+    rows of hidden (default: all).
 
-    hidden (rows, hidden_size) and weight (vocab, hidden_size) are bf16 or f16 CUDA tensors
+    hidden (n, hidden_size) and weight (vocab, hidden_size) are bf16 or f16 CUDA tensors
     with contiguous rows; the logits are rounded to their dtype before the argmax (the LM
-    head's own output type) and never written. ``workspace`` is a uint8 CUDA tensor of at
-    least ``lm_head_argmax_workspace_size(rows)`` bytes, zero before its first use (each
-    launch leaves it zero). Returns the int64 ids, or None when the dtype or shape is
-    outside what the kernel takes (the caller then computes logits).
+    head's own output type) and never written. The kernel takes rows in tiles of 128: a
+    hidden whose n is a multiple of 128 is used as it is (rows past ``rows`` are computed
+    and dropped), any other is copied into a zero-padded one first. ``workspace`` is a uint8
+    CUDA tensor of at least ``lm_head_argmax_workspace_size(n rounded up to 128)`` bytes,
+    zero before its first use (each launch leaves it zero). Returns the int64 ids of the
+    first ``rows`` rows, or None when the dtype or shape is outside what the kernel takes
+    (the caller then computes logits).
     """
     _require_cuda("hidden", hidden)
     _require_cuda("weight", weight)
@@ -335,22 +341,38 @@ def lm_head_argmax(
         raise ValueError("hidden and weight dtypes differ")
     if hidden.stride(1) != 1 or weight.stride(1) != 1:
         raise ValueError("hidden and weight rows must be contiguous")
-    rows, size = hidden.shape
-    if hidden.dtype not in (torch.bfloat16, torch.float16):
+    if hidden.dtype not in (torch.bfloat16, torch.float16) or hidden.shape[1] % 64:
         return None
+    n = hidden.shape[0]
+    rows = n if rows is None else rows
+    if not 0 <= rows <= n:
+        raise ValueError("rows must lie within hidden's rows")
+    if n % 128:
+        padded = hidden.new_zeros((n + (-n) % 128, hidden.shape[1]))
+        padded[:n] = hidden
+        hidden = padded
+    n = hidden.shape[0]
     dev = hidden.device
-    if out_ids is None:
-        out_ids = torch.empty(rows, dtype=torch.int64, device=dev)
-    if out_ids.dtype != torch.int64 or out_ids.numel() < rows or not out_ids.is_contiguous():
-        raise ValueError("out_ids must be a contiguous int64 tensor of at least rows entries")
-    if out_max is not None and (out_max.dtype != torch.float32 or out_max.numel() < rows):
-        raise ValueError("out_max must be a float32 tensor of at least rows entries")
+    for name, t, dt in (("out_ids", out_ids, torch.int64), ("out_max", out_max, torch.float32)):
+        if t is not None and (t.dtype != dt or not t.is_contiguous() or t.numel() < rows):
+            raise ValueError(f"{name} must be a contiguous {dt} tensor of at least rows entries")
+    # the kernel writes one entry per padded row: the caller's tensors when they are large
+    # enough, else scratch whose first rows are copied back
+    ids = out_ids if out_ids is not None and out_ids.numel() >= n else \
+        torch.empty(n, dtype=torch.int64, device=dev)
+    mx = out_max if out_max is None or out_max.numel() >= n else \
+        torch.empty(n, dtype=torch.float32, device=dev)
     rc = _lib.load().b2p_lm_head_argmax(
-        hidden.data_ptr(), hidden.stride(0), weight.data_ptr(), weight.stride(0), rows,
-        weight.shape[0], size, dtype_code(hidden.dtype), out_ids.data_ptr(), _ptr(out_max),
-        workspace.data_ptr(), workspace.numel(), _ptr(err_flag), _stream(dev),
+        hidden.data_ptr(), hidden.stride(0), weight.data_ptr(), weight.stride(0), n,
+        weight.shape[0], hidden.shape[1], dtype_code(hidden.dtype), ids.data_ptr(),
+        _ptr(mx), workspace.data_ptr(), workspace.numel(), _ptr(err_flag), _stream(dev),
     )
     if rc == _lib.B2P_EUNSUPPORTED:
         return None
     _lib.check(rc, "b2p_lm_head_argmax")
-    return out_ids[:rows]
+    if out_ids is not None and ids is not out_ids:
+        out_ids[:rows].copy_(ids[:rows])
+        ids = out_ids
+    if out_max is not None and mx is not out_max:
+        out_max[:rows].copy_(mx[:rows])
+    return ids[:rows]

@@ -276,6 +276,7 @@ class B200PagedModelRunner:
         self._workspace = torch.zeros(16, dtype=torch.uint8, device=self._device)
         self._err = torch.zeros(1, dtype=torch.int32, device=self._device)
         self._mirror: _TableMirror | None = None
+        self._k6_hidden: torch.Tensor | None = None
         self._k6_workspace: torch.Tensor | None = None
 
     # ------------------------------------------------------------------ host metadata
@@ -421,15 +422,24 @@ class B200PagedModelRunner:
         if head is None:
             return None
         n = len(executions)
-        if self._k6_workspace is None or self._k6_workspace.numel() < _ops.lm_head_argmax_workspace_size(n):
-            self._k6_workspace = torch.zeros(_ops.lm_head_argmax_workspace_size(max(n, 256)),
-                                             dtype=torch.uint8, device=self._device)
+        padded = n + (-n) % 128  # K6 takes rows in tiles of 128
+        if self._k6_hidden is None or self._k6_hidden.shape[0] < padded:
+            self._k6_hidden = torch.zeros((max(padded, 256), head.shape[1]), dtype=head.dtype,
+                                          device=self._device)
+            self._k6_workspace = torch.zeros(
+                _ops.lm_head_argmax_workspace_size(self._k6_hidden.shape[0]), dtype=torch.uint8,
+                device=self._device)
+
         def run(batch, input_ids, cache):
             out = self._model.model(input_ids=input_ids.unsqueeze(0),
                                     position_ids=batch.positions.unsqueeze(0), attention_mask=None,
                                     past_key_values=cache, use_cache=True)
-            hidden = out.last_hidden_state[0].index_select(0, batch.logit_indices)
-            return _ops.lm_head_argmax(hidden, head, self._k6_workspace, err_flag=self._err)
+            # last rows into the padded buffer (rows past n hold earlier steps' states, whose
+            # ids are computed and dropped)
+            hidden = self._k6_hidden[:padded]
+            torch.index_select(out.last_hidden_state[0], 0, batch.logit_indices, out=hidden[:n])
+            return _ops.lm_head_argmax(hidden, head, self._k6_workspace, err_flag=self._err,
+                                       rows=n)
         return self._run(executions, run)
 
     def _lm_head(self) -> torch.Tensor | None:
