@@ -8,15 +8,17 @@
 // index, so the (B, 151936) logits never reach HBM:
 //
 //   logits tile = H (smem, K-major: rows x hidden) x W^T (smem, K-major: vocab x hidden),
-//                 tcgen05.mma kind::f16, M = 128 rows, N = 256 vocab entries, fp32 in TMEM
+//                 tcgen05.mma kind::f16, M = 128 rows, N <= 256 vocab entries, fp32 in TMEM
 //   per row: max and first arg-max over the tile, each logit rounded to the model dtype
 //            first (the reference's LM head returns bf16/f16 logits and takes argmax of
 //            those, ties to the lowest index)
 //
-// Work item = (group of up to 256 rows, 256-entry vocab tile); the two 128-row halves of a
-// group share each W tile (one W read per group), and each hidden chunk serves 256 vocab
-// entries (N = 256 MMAs: half the instructions and hidden re-reads of N = 128 ones, which
-// measured 1.4x slower). Persistent CTAs walk the items round
+// Work item = (group of up to 256 rows, vocab tile of N entries); the two 128-row halves of
+// a group share each W tile (one W read per group), and each hidden chunk serves N vocab
+// entries. N (a multiple of 16, at most 256) is chosen per launch so that the items split
+// evenly over the SMs: 208 for a 151936-entry vocabulary on 148 SMs (731 items, 4.94 per
+// SM) where N = 256 leaves two SMs a fifth 256-entry item. Wide tiles matter: with N = 128
+// the MMAs of two row halves measured 1.4x slower. Persistent CTAs walk the items round
 // robin; each keeps a running best per row while its items stay in one row group and
 // merges it into a per-row 64-bit key with atomicMax (value in the high word, ordered so
 // that larger logits give larger keys; ~index in the low word, so equal values keep the
@@ -38,7 +40,7 @@ namespace {
 using namespace b2p;
 
 constexpr int kRowsTile = 128;   // rows per MMA (TMEM lanes)
-constexpr int kVocabTile = 256;  // vocab entries per MMA (N)
+constexpr int kVocabTile = 256;  // largest vocab tile (MMA N)
 constexpr int kGroupRows = 2 * kRowsTile;
 constexpr int kStages = 3;
 constexpr int kThreads = 192;
@@ -51,7 +53,8 @@ struct LmHeadParams {
   int64_t vocab;
   int hidden;            // multiple of 64
   int n_groups;          // ceil(rows / 256)
-  int64_t n_vtiles;      // ceil(vocab / 256)
+  int n_tile;            // vocab entries per item (multiple of 16, <= 256)
+  int64_t n_vtiles;      // ceil(vocab / n_tile)
   unsigned long long* keys;  // [rows], zero between launches
   int32_t* ctr;          // CTAs done, zero between launches
   int64_t* out_ids;      // [rows]
@@ -152,10 +155,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           uint8_t* st = smem + s * Plan::kStageBytes;
-          mbar_arrive_expect_tx(&full[s], (uint32_t)(halves * kChunkBytes + Plan::kWBytes));
+          mbar_arrive_expect_tx(&full[s], (uint32_t)(halves * kChunkBytes + p.n_tile * 128));
           for (int h = 0; h < halves; ++h)
             tma_load_4d(st + h * kChunkBytes, &hmap, &full[s], 0, kc, 0, row0 + h * kRowsTile);
-          tma_load_4d(st + 2 * kChunkBytes, &wmap, &full[s], 0, kc, 0, (int)(vt * kVocabTile));
+          tma_load_4d(st + 2 * kChunkBytes, &wmap, &full[s], 0, kc, 0, (int)(vt * p.n_tile));
         }
       }
       if (!ok) *abort_flag = 1;
@@ -167,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(ab, kRowsTile, kVocabTile, 0, 0);
+      const uint32_t idesc = idesc_f16(ab, kRowsTile, p.n_tile, 0, 0);
       const uint64_t d0 = smem_desc_sw128(smem_u32(smem), 16, 1024);
       int64_t q = 0;
       int li = 0;  // items of this CTA (accumulator phases)
@@ -243,15 +246,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         cur_grp = grp;
       }
       tc_fence_after();
-      const int64_t col0 = vt * kVocabTile;
+      const int64_t col0 = vt * p.n_tile;
       for (int h = 0; h < halves; ++h) {
 #pragma unroll 1
-        for (int c0 = 0; c0 < kVocabTile; c0 += 32) {
+        for (int c0 = 0; c0 < p.n_tile; c0 += 32) {
           uint32_t v[32];
           tmem_ld32(lane_base + 256u * h + c0, v);
           tmem_wait_ld();
-          // columns past the vocabulary hold the zero-filled W rows' products: skip them
-          const int64_t left = p.vocab - (col0 + c0);
+          // columns past the tile (a 16-column tail) or past the vocabulary (zero-filled W
+          // rows) hold no logits of this item: skip them
+          const int64_t left = min((int64_t)(p.n_tile - c0), p.vocab - (col0 + c0));
           const int nvalid = left < 32 ? (int)left : 32;
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
@@ -330,19 +334,34 @@ int b2p_lm_head_argmax(const void* hidden, int64_t hidden_row_stride,
   if (workspace_bytes < b2p_lm_head_argmax_workspace_size(rows) ||
       (reinterpret_cast<uintptr_t>(workspace) & 7u))
     return B2P_EWORKSPACE;
+  // vocab tile: the multiple of 16 (<= 256) that minimises the most vocab entries one SM
+  // processes, ceil(items / SMs) * N; on ties the wider tile
+  const int n_groups = (rows + kGroupRows - 1) / kGroupRows;
+  const int64_t sms = b2p_host::sm_count();
+  int n_tile = kVocabTile;
+  int64_t best = INT64_MAX;
+  for (int n = kVocabTile; n >= 16; n -= 16) {
+    const int64_t items = (int64_t)n_groups * ((vocab + n - 1) / n);
+    const int64_t cost = (items + sms - 1) / sms * n;
+    if (cost < best) {
+      best = cost;
+      n_tile = n;
+    }
+  }
   CUtensorMap hmap, wmap;
   int rc = b2p_host::tensor_map_4d_rows(&hmap, hidden, rows, 1, hidden_size, hidden_row_stride,
                                         hidden_size, 2, kRowsTile);
   if (rc != B2P_OK) return rc;
   rc = b2p_host::tensor_map_4d_rows(&wmap, weight, vocab, 1, hidden_size, weight_row_stride,
-                                    hidden_size, 2, kVocabTile);
+                                    hidden_size, 2, n_tile);
   if (rc != B2P_OK) return rc;
   LmHeadParams p;
   p.rows = rows;
   p.vocab = vocab;
   p.hidden = hidden_size;
-  p.n_groups = (rows + kGroupRows - 1) / kGroupRows;
-  p.n_vtiles = (vocab + kVocabTile - 1) / kVocabTile;
+  p.n_groups = n_groups;
+  p.n_tile = n_tile;
+  p.n_vtiles = (vocab + n_tile - 1) / n_tile;
   p.keys = static_cast<unsigned long long*>(workspace);
   p.ctr = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + (size_t)rows * 8);
   p.out_ids = out_ids;
