@@ -264,12 +264,16 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   // Programmatic dependent launch: this grid may be scheduled while the previous kernel on
-  // the stream is finishing. It reads and writes no global memory before that kernel has
-  // completed and its writes are visible (the wait), and it lets the next launch on the
-  // stream get scheduled the same way (the trigger). Only the launch and scheduling of the
-  // CTAs overlap; with a predecessor that never triggers, the wait returns at once.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // the stream is finishing, and lets the next launch be scheduled the same way (the
+  // trigger). Before the wait it reads only the context lengths and block tables (to find
+  // its range and resolve its first blocks), which no kernel that triggers early writes:
+  // this one never writes them, and a kernel that does not trigger (block-table builds,
+  // host copies, PyTorch ops) has completed before this grid starts. Errors found there go
+  // to the error word with atomic ORs, which commute. The pool, the outputs and the
+  // workspace are touched only after the wait, once the previous kernel has completed and
+  // its writes are visible.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  auto pdl_wait = []() { asm volatile("griddepcontrol.wait;" ::: "memory"); };
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   // Warps w and w+1 (2 KV heads) or w..w+3 (4 heads) stream the same sub-blocks for
@@ -309,6 +313,7 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
   const int64_t unit = (int64_t)blockIdx.x * units_per_cta + warp / hpu;
   find_range(p, (int64_t)gridDim.x * units_per_cta, unit, r);
   if (r.begin >= r.end) {
+    pdl_wait();
     if (empties_warp) write_empties();
     return;
   }
@@ -354,6 +359,7 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
     }
     issued = k + 1;
   };
+  pdl_wait();  // the first access to memory the previous kernel may write
   for (int64_t k = 0; k < S && k < n; ++k) issue(k);
   if (empties_warp) write_empties();  // while the first tiles are in flight
   if (n > 32) slot_hi = res(p, 32, lane, num_slots);
