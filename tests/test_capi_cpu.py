@@ -48,3 +48,28 @@ def test_argument_errors_need_no_gpu():
                               1.0, None, 0, 0, None, 0, 0, None, None)
     assert rc == _lib.B2P_EINVAL
     assert lib.b2p_paged_decode_workspace_size(256, 12, 2, 128) > 0
+
+
+def test_lm_head_argmax_rejections_need_no_gpu():
+    """K6's argument, shape and workspace checks answer before any CUDA call."""
+    from llm_engineering_b200 import _lib
+
+    lib = _lib.load()
+    assert lib.b2p_lm_head_argmax_workspace_size(256) == 256 * 8 + 16
+    fake = 1 << 20  # an aligned non-null address; nothing is dereferenced on these paths
+    # nothing to do
+    assert lib.b2p_lm_head_argmax(None, 0, None, 0, 0, 1000, 128, 0, fake, None, None, 0,
+                                  None, None) == _lib.B2P_OK
+    # negative rows / missing pointers
+    assert lib.b2p_lm_head_argmax(fake, 128, fake, 128, -1, 1000, 128, 0, fake, None, fake,
+                                  4096, None, None) == _lib.B2P_EINVAL
+    assert lib.b2p_lm_head_argmax(None, 128, fake, 128, 128, 1000, 128, 0, fake, None, fake,
+                                  4096, None, None) == _lib.B2P_EINVAL
+    # fp32, hidden size not a multiple of 64, rows not in 128-row tiles
+    for dtype, hidden, rows in ((2, 128, 128), (0, 100, 128), (0, 128, 100)):
+        assert lib.b2p_lm_head_argmax(fake, hidden, fake, hidden, rows, 1000, hidden, dtype,
+                                      fake, None, fake, 1 << 16, None,
+                                      None) == _lib.B2P_EUNSUPPORTED
+    # workspace smaller than the rows need
+    assert lib.b2p_lm_head_argmax(fake, 128, fake, 128, 256, 1000, 128, 0, fake, None, fake,
+                                  256 * 8, None, None) == _lib.B2P_EWORKSPACE
