@@ -1,6 +1,6 @@
 """GPU parity of the four kernels against the CPU oracle (called through the C ABI).
 
-Tolerances: bf16/f16 attention within max-abs 2e-2 and
+Tolerances (the parity contract of this path): bf16/f16 attention within max-abs 2e-2 and
 mean-abs 2e-3 of the fp32 oracle; fp32 attention within 1e-4; KV writes and metadata
 bit-exact.
 """

@@ -248,7 +248,7 @@ def test_bf16_engine_through_tensor_core_kernels_config1_requests():
 
     * Every attention call of every layer and step is checked against the oracle's fp32
       attention over the same bf16 queries and pool contents (after the step's K/V writes):
-      max-abs 2e-2 and mean-abs 2e-3, the north-star bounds.
+      max-abs 2e-2 and mean-abs 2e-3, the parity bounds of this path.
     * Logits, every step, against the reference-style packed runner (gather + dense mask
       + SDPA) in fp32 on the same weights: within 1.5x the distance of that same runner in
       bf16 (the bf16 budget of the reference path itself), and the same top-1 token on
