@@ -81,7 +81,7 @@ K3_TRAFFIC_BYTES: float | None = 328.702464e6
 # The same for K2 on the long-context workload, from a capture over a one-layer pool with
 # the same sequences and tables (per-launch traffic does not depend on the pool's layer
 # count): 2,599.38 MB read + 9.10 MB written.
-LC_K2_TRAFFIC_BYTES: float | None = 2.608486e9
+LC_K2_TRAFFIC_BYTES: float | None = 2.602907e9
 # Prompt groups of the prefill e2e leg (copies of one group overlap another's compute).
 E2E_GROUPS = 4
 SUSTAIN_S = 2.0  # length of the sustained-clock window after the timed region
