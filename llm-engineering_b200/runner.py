@@ -491,13 +491,15 @@ class B200PagedModelRunner:
         """Bits the kernels reported since the last call (0 = none); clears them.
 
         After a bounded wait gave up (``B2P_DEV_WAIT_TIMEOUT``) a launch may have left
-        split-K counters set: the decode workspace and the prefill claim counters are then
-        zeroed before the next step."""
+        split-K counters or greedy-pick keys set: the decode workspace, the K6 workspace and
+        the prefill claim counters are then zeroed before the next step."""
         v = int(self._err.item())
         if v:
             self._err.zero_()
             if v & DEV_WAIT_TIMEOUT:
                 self._workspace.zero_()
+                if self._k6_workspace is not None:
+                    self._k6_workspace.zero_()
                 reset = getattr(_ops, "reset_scratch", None)
                 if reset is not None:
                     reset(self._device)

@@ -244,3 +244,29 @@ def test_block_table_mirror_tracks_appends_readmissions_and_growth():
         for row, blocks in zip(rows, lists):
             assert mirror.table[row, :len(blocks)].tolist() == list(blocks)
     assert mirror.table.shape[0] >= 12 and mirror.table.shape[1] > 2
+
+
+def test_wait_timeout_resets_every_scratch_buffer(monkeypatch):
+    """After a bounded wait gave up (B2P_DEV_WAIT_TIMEOUT) a launch may have left split-K
+    counters or greedy-pick keys set: device_error() zeroes the decode workspace and the K6
+    workspace and resets the prefill claim counters, then reports the bits once."""
+    from llm_engineering_b200._lib import DEV_BLOCK_RANGE, DEV_WAIT_TIMEOUT
+
+    kc, vc = pool(2, 8, 4, 2, 16)
+    ours = B200PagedModelRunner(tiny_model(), torch.device("cpu"), _Storage(kc, vc, 4))
+    resets = []
+    monkeypatch.setattr(runner_mod._ops, "reset_scratch", lambda dev: resets.append(dev),
+                        raising=False)
+    ours._workspace.fill_(7)
+    ours._k6_workspace = torch.full((64,), 3, dtype=torch.uint8)
+    ours._err.fill_(DEV_WAIT_TIMEOUT | DEV_BLOCK_RANGE)
+    assert ours.device_error() == DEV_WAIT_TIMEOUT | DEV_BLOCK_RANGE
+    assert int(ours._workspace.count_nonzero()) == 0
+    assert int(ours._k6_workspace.count_nonzero()) == 0
+    assert resets == [torch.device("cpu")]
+    assert ours.device_error() == 0  # the bits were cleared
+    # a block-range error alone leaves the scratch buffers as they are
+    ours._workspace.fill_(7)
+    ours._err.fill_(DEV_BLOCK_RANGE)
+    assert ours.device_error() == DEV_BLOCK_RANGE
+    assert int(ours._workspace.count_nonzero()) == ours._workspace.numel()
