@@ -48,6 +48,9 @@ class Scheduler:
         self.block_table = BlockTable(pool=self.block_pool, block_size=configuration.block_size)
         self._waiting: deque[SequenceState] = deque()
         self._running: list[SequenceState] = []
+        # identities of the running sequences: membership checks in O(1) (the list keeps
+        # the admission order that preemption and the step's execution order follow)
+        self._running_ids: set[int] = set()
         self._finished: list[SequenceState] = []
         self._ids: set[str] = set()
         self._num_preemptions = 0
@@ -128,6 +131,7 @@ class Scheduler:
         self._waiting.popleft()
         seq.mark_running()
         self._running.append(seq)
+        self._running_ids.add(id(seq))
 
     def schedule(self) -> SchedulerOutput:
         if self.configuration.enable_chunked_prefill:
@@ -197,7 +201,7 @@ class Scheduler:
     def reserve_generated_token(self, sequence: SequenceState) -> None:
         if sequence.is_finished:
             raise RuntimeError("Cannot reserve KV-cache storage for a finished sequence.")
-        if not any(s is sequence for s in self._running):
+        if id(sequence) not in self._running_ids:
             raise RuntimeError(
                 "Cannot reserve KV-cache storage for a sequence that is not running.")
         rid = sequence.request.request_id
@@ -217,7 +221,7 @@ class Scheduler:
     def finish_sequence(self, sequence: SequenceState, reason: FinishReason) -> None:
         if sequence.is_finished:
             raise RuntimeError("Cannot finish a sequence that is already finished.")
-        if not any(s is sequence for s in self._running):
+        if id(sequence) not in self._running_ids:
             raise RuntimeError("Cannot finish a sequence that is not running.")
         self._release(sequence)
         sequence.mark_finished(reason)
@@ -228,11 +232,12 @@ class Scheduler:
         self.block_table.free_request(seq.request.request_id)
         self._prefilled.pop(seq.request.request_id, None)
         self._running = [s for s in self._running if s is not seq]
+        self._running_ids.discard(id(seq))
 
     def _preempt(self, seq: SequenceState) -> None:
         if seq.is_finished:
             raise RuntimeError("Cannot preempt a finished sequence.")
-        if not any(s is seq for s in self._running):
+        if id(seq) not in self._running_ids:
             raise RuntimeError("Cannot preempt a sequence that is not running.")
         self._release(seq)
         seq.mark_preempted()
