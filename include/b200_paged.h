@@ -124,8 +124,12 @@ B2P_API int b2p_kv_write(const void* keys, int64_t k_tok_stride, int64_t k_head_
  *                  K/V must already be in the pool, as after PagedKVCache's scatter)
  *   out          : [num_seqs, num_q_heads, head_dim] (strides in elements)
  *   workspace    : device scratch of b2p_paged_decode_workspace_size() bytes, zero-filled
- *                  once by the caller before its first use; the kernel leaves it
- *                  zero-filled again after every launch that completes.
+ *                  once by the caller before its first use. It holds the split partial
+ *                  records, then the count-in counters at an offset fixed by the launch
+ *                  shape (heads, head_dim, dtype); every launch that completes leaves the
+ *                  counters zero, so launches of one shape reuse it with any num_seqs up
+ *                  to the size it was queried for. Zero it again before a launch of
+ *                  another shape, and after a launch that set B2P_DEV_WAIT_TIMEOUT.
  * Scores are q.k * scale (scale = head_dim^-0.5 for Qwen2, modeling_qwen2.py:199).
  */
 B2P_API size_t b2p_paged_decode_workspace_size(int num_seqs, int num_q_heads, int num_kv_heads,

@@ -877,13 +877,23 @@ int64_t ctas_x(int ctas_per_sm, int num_kv_heads, int hpu) {
   return c < 1 ? 1 : c;
 }
 
+// Workspace layout: the partial records first (their size depends only on the launch
+// shape: heads, head_dim, group, dtype and SM occupancy), then one count-in counter per
+// (kv head, sequence). The counters therefore sit at the same offset for every launch of a
+// shape, in bytes that only counters ever use; every launch that completes leaves them zero
+// (each last contributor re-zeroes its own). Counters placed first, sized by this launch's
+// sequence count, would grow into bytes that an earlier launch with fewer sequences filled
+// with partial records, and a stale non-zero count there never reaches the merge.
 size_t counters_bytes(int num_seqs, int num_kv_heads) {
   return ((size_t)num_kv_heads * num_seqs * 4 + 255) & ~size_t(255);
 }
 
+size_t partials_bytes(int num_kv_heads, int64_t units, int record) {
+  return ((size_t)num_kv_heads * units * 2 * record * sizeof(float) + 255) & ~size_t(255);
+}
+
 size_t workspace_bytes(int num_seqs, int num_kv_heads, int64_t units, int record) {
-  return counters_bytes(num_seqs, num_kv_heads) +
-         (size_t)num_kv_heads * units * 2 * record * sizeof(float);
+  return partials_bytes(num_kv_heads, units, record) + counters_bytes(num_seqs, num_kv_heads);
 }
 
 }  // namespace
@@ -960,7 +970,8 @@ struct DecodeRoute {
   Plan pl;
   int hpu = 1;
   int64_t ctas = 0;
-  size_t need = 0;  // workspace bytes of the tensor-core kernel
+  size_t need = 0;         // workspace bytes of the tensor-core kernel
+  size_t counters_at = 0;  // byte offset of the counters (after the partial records)
 };
 
 int decode_route(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
@@ -997,8 +1008,9 @@ int decode_route(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
   if (rc != B2P_OK) return rc;
   rt.hpu = heads_per_unit(num_kv_heads, rt.pl.warps);
   rt.ctas = ctas_x(rt.pl.ctas_per_sm, num_kv_heads, rt.hpu);
-  rt.need = workspace_bytes(num_seqs, num_kv_heads, rt.ctas * (rt.pl.warps / rt.hpu),
-                            rt.pl.record);
+  const int64_t units = rt.ctas * (rt.pl.warps / rt.hpu);
+  rt.need = workspace_bytes(num_seqs, num_kv_heads, units, rt.pl.record);
+  rt.counters_at = partials_bytes(num_kv_heads, units, rt.pl.record);
   return B2P_OK;
 }
 
@@ -1077,9 +1089,8 @@ int decode_impl(const void* q, int64_t q_tok_stride, int64_t q_head_stride,
   p.block_size = block_size;
   p.num_blocks = num_slots / block_size;
   p.scale_log2 = scale * kLog2e;
-  p.counters = static_cast<int32_t*>(workspace);
-  p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
-                                        counters_bytes(num_seqs, num_kv_heads));
+  p.partials = static_cast<float*>(workspace);
+  p.counters = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + rt.counters_at);
   p.err = err_flag;
   p.new_k = static_cast<const uint8_t*>(app.k);
   p.nk_tok = app.k_tok;
@@ -1215,7 +1226,8 @@ extern "C" int b2p_paged_decode_noalloc(const void* q, int64_t q_tok_stride,
     rc = noalloc_scratch(&scratch);
     if (rc != B2P_OK) return rc;
     // The array keeps whatever the previous call left; the counters must start at zero.
-    const cudaError_t e = cudaMemsetAsync(scratch, 0, counters_bytes(num_seqs, num_kv_heads),
+    const cudaError_t e = cudaMemsetAsync(static_cast<uint8_t*>(scratch) + rt.counters_at, 0,
+                                          counters_bytes(num_seqs, num_kv_heads),
                                           static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return b2p_host::record_error(e);
   }
