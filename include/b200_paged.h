@@ -271,6 +271,9 @@ B2P_API int b2p_build_metadata(const int32_t* query_lens, const int32_t* context
  * given row strides (elements), 16-byte aligned; hidden_size a multiple of 64 and rows a
  * multiple of 128 (pad the hidden rows; the ids of padding rows are computed and unused).
  * out_max (optional, nullable) receives the rounded maximum logit of each row.
+ * NaN logits are passed over: a row whose logits are all NaN or -inf (as a NaN hidden row
+ * gives) gets id 0 and maximum NaN, torch's id for it, so every id is a valid token; a row
+ * with some NaN logits gets the largest of the others (torch would return the first NaN).
  * workspace: b2p_lm_head_argmax_workspace_size(rows) bytes, 8-byte aligned and zero before
  * the first launch; every launch that runs to its end leaves it zero again.
  * Returns B2P_EUNSUPPORTED for other dtypes or shapes (the caller keeps its logits path),

@@ -293,8 +293,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     __threadfence();
     for (int r = threadIdx.x; r < p.rows; r += blockDim.x) {
       const unsigned long long key = __ldcg(p.keys + r);
-      p.out_ids[r] = key ? (int64_t)(0xffffffffu - (uint32_t)(key & 0xffffffffu)) : -1;
-      if (p.out_max) p.out_max[r] = key ? from_order_bits((uint32_t)(key >> 32)) : -INFINITY;
+      // No logit of the row compared above -inf: every one is NaN or -inf (a NaN hidden
+      // row makes them all NaN). torch's argmax gives index 0 for such a row; so does this,
+      // and the id is always a valid token.
+      p.out_ids[r] = key ? (int64_t)(0xffffffffu - (uint32_t)(key & 0xffffffffu)) : 0;
+      if (p.out_max) p.out_max[r] = key ? from_order_bits((uint32_t)(key >> 32))
+                                 : __int_as_float(0x7fffffff);
       p.keys[r] = 0;
     }
     if (threadIdx.x == 0) *p.ctr = 0;

@@ -649,12 +649,14 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
           }
           mma_commit(&o_done[h]);
         };
-        // S of head h is free once the PV MMA of its previous tile has read P (head_dim
-        // 128: P overwrites S), or once the softmax has read the previous S (head_dim 64).
+        // S of head h may be overwritten once the softmax has read the previous S (head_dim
+        // 64, where P has columns of its own). With head_dim 128, P overwrites S and the
+        // next QK^T only has to come after the PV that reads P, which the tensor pipe
+        // guarantees for MMAs issued in that order by this thread.
         auto s_free = [&](int h) -> bool {
           const int n = h ? n1 : n0;
-          return n == 0 || mbar_wait_bounded(D == 64 ? &s_read[h] : &o_done[h],
-                                             (uint32_t)((n - 1) & 1), p.err);
+          if constexpr (D != 64) return true;
+          return n == 0 || mbar_wait_bounded(&s_read[h], (uint32_t)((n - 1) & 1), p.err);
         };
         ok = mbar_wait_bounded(q_full, (uint32_t)(nq & 1), p.err);
         if (ok) ok = mbar_wait_bounded(&k_full[g & 1], (uint32_t)((g >> 1) & 1), p.err);
@@ -714,9 +716,11 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
               issue_pv(h, g, j == 0);
               if (h) ++n1; else ++n0;
               if (more) {
+                // QK_h(j+1) overwrites the S columns that hold P_h(j), which PV_h(j) just
+                // issued reads: both MMAs come from this thread and the tensor pipe runs
+                // them in issue order, so no wait for PV_h(j) to complete is needed here.
                 if (h == 0)
                   ok = mbar_wait_bounded(&k_full[(g + 1) & 1], (uint32_t)(((g + 1) >> 1) & 1), p.err);
-                ok = ok && s_free(h);
                 if (!ok) break;
                 tc_fence_after();
                 issue_qk(h, g + 1);

@@ -75,6 +75,22 @@ def test_lm_head_argmax_ties_go_to_the_lowest_index(ops):
     assert torch.equal(ids, want)
 
 
+def test_lm_head_argmax_nan_row_gets_a_valid_token(ops):
+    """A NaN hidden row makes every logit of the row NaN: its id is 0, as torch's argmax
+    gives, never an invalid token; the other rows are unaffected."""
+    rows, vocab, hidden = 6, 5000, 256
+    h, w = _inputs(rows, vocab, hidden, torch.bfloat16, seed=11)
+    h[2] = float("nan")
+    ws = torch.zeros(ops.lm_head_argmax_workspace_size(rows), dtype=torch.uint8, device="cuda")
+    out_max = torch.empty(rows, dtype=torch.float32, device="cuda")
+    ids = ops.lm_head_argmax(h, w, ws, out_max=out_max)
+    want = (h @ w.T).float().argmax(-1)
+    assert int(ids[2]) == int(want[2]) == 0
+    assert bool(out_max[2].isnan())
+    keep = [0, 1, 3, 4, 5]
+    assert torch.equal(ids[keep], want[keep])
+
+
 def test_lm_head_argmax_unsupported_shapes_return_none(ops):
     h = torch.randn(4, 100, device="cuda").to(torch.bfloat16)  # hidden not a multiple of 64
     w = torch.randn(50, 100, device="cuda").to(torch.bfloat16)
