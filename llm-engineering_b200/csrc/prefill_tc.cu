@@ -631,19 +631,25 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_tc(const __grid_consta
           const uint32_t q_addr = smem_u32(smem + L::kOffQ + h * L::kQBytes);
           const uint32_t k_addr = smem_u32(smem + L::kOffK + (int)(gg & 1) * L::kKVBytes);
           const uint32_t d = tbase + col_s(h);
+          // base descriptors once; each K step adds its byte offset / 16 to the address
+          // field (shared-memory addresses stay below 2^18 bytes, so the field never
+          // carries into the next one)
+          const uint64_t qa = smem_desc_sw128(q_addr, 16, 1024);
+          const uint64_t kb = smem_desc_sw128(k_addr, 16, 1024);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
-            const uint64_t da = smem_desc_sw128(q_addr + (kk >> 2) * (kM * 128) + (kk & 3) * 32, 16, 1024);
-            const uint64_t db = smem_desc_sw128(k_addr + (kk >> 2) * (kN * 128) + (kk & 3) * 32, 16, 1024);
+            const uint64_t da = qa + (uint64_t)(((kk >> 2) * (kM * 128) + (kk & 3) * 32) >> 4);
+            const uint64_t db = kb + (uint64_t)(((kk >> 2) * (kN * 128) + (kk & 3) * 32) >> 4);
             mma_ss(d, da, db, id_qk, kk > 0 ? 1u : 0u);
           }
           mma_commit(&s_full[h]);
         };
         auto issue_pv = [&](int h, int64_t gg, bool first) {
           const uint32_t v_addr = smem_u32(smem + L::kOffV + (int)(gg & 1) * L::kKVBytes);
+          const uint64_t vb = smem_desc_sw128(v_addr, kN * 128, 1024);
 #pragma unroll
           for (int kk = 0; kk < kN / 16; ++kk) {
-            const uint64_t db = smem_desc_sw128(v_addr + kk * (16 * 128), kN * 128, 1024);
+            const uint64_t db = vb + (uint64_t)((kk * (16 * 128)) >> 4);
             mma_ts(tbase + col_o<D>(h), tbase + col_p_keys<D>(h, kk), db, id_pv,
                    (!first || kk > 0) ? 1u : 0u);
           }
