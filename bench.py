@@ -76,8 +76,8 @@ sys.path.insert(0, str(REPO))
 # over the same sequences and block tables: 616.26 MB read + 6.43 MB written.
 K2_TRAFFIC_BYTES: float | None = 622.695936e6
 # The same for K3 on the 32-prompt prefill workload, from one ncu capture of a K3 launch:
-# 212.84 MB read + 117.06 MB written.
-K3_TRAFFIC_BYTES: float | None = 329.907968e6
+# 213.62 MB read + 115.96 MB written.
+K3_TRAFFIC_BYTES: float | None = 329.581568e6
 # The same for K2 on the long-context workload, from a capture over a one-layer pool with
 # the same sequences and tables (per-launch traffic does not depend on the pool's layer
 # count): 2,599.38 MB read + 9.10 MB written.
