@@ -19,6 +19,9 @@
 // Tensor memory holds S_A, S_B, O_A, O_B (512 columns, one CTA per SM). The MMA warp
 // issues PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1), ..., so the softmax of one head runs
 // while the tensor cores work on the other head, and both heads read each K/V tile once.
+// QK_h(j+1) follows PV_h(j) with no wait for it to complete: the tensor pipe runs the MMAs
+// of the issuing thread in order, so PV_h(j) has read P_h(j) before QK_h(j+1) overwrites
+// those columns of S_h.
 // With head_dim 64 the order is QK_A(j+1), QK_B(j+1), PV_A(j), PV_B(j): P has columns of
 // its own there, so the next QK^T only waits for the softmax to have read S.
 // K/V tiles of 128 tokens are assembled from eight 16-slot pool sub-blocks (TMA tile
