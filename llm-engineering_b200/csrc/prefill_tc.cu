@@ -110,9 +110,11 @@ struct Plan {
 };
 
 // TMEM columns (512 allocated): S of head A at 0, of head B at 128. head_dim 128: O_A at
-// 256, O_B at 384, and P overwrites the second half of its S (columns +64 .. +127, two keys
-// per column). head_dim 64: O_A at 256, O_B at 320, and P has columns of its own (P_A at
-// 384, P_B at 448), so S is free for the next QK^T as soon as the softmax has read it.
+// 256, O_B at 384, and P overwrites part of its S: each key half's softmax warp writes its
+// 64 keys' P (two keys per column) over the first 32 of that half's own 64 S columns (S + 0
+// .. 31 for keys 0..63, S + 64 .. 95 for keys 64..127; see col_p_keys). head_dim 64: O_A at
+// 256, O_B at 320, and P has columns of its own (P_A at 384, P_B at 448), so S is free for
+// the next QK^T as soon as the softmax has read it.
 constexpr uint32_t kTmemCols = 512;
 __device__ __forceinline__ uint32_t col_s(int h) { return h ? 128u : 0u; }
 template <int D>
