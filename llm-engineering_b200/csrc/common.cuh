@@ -90,6 +90,17 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// Prefetch of one 5-D tensor-map box into L2 only: no shared-memory destination and no
+// completion to wait for. L2 is where every kernel's global writes land, so a prefetch of
+// data that another kernel still writes cannot make a later read see stale values.
+__device__ __forceinline__ void tma_prefetch_l2_5d(const CUtensorMap* map, int c0, int c1, int c2,
+                                                   int c3, int c4) {
+  asm volatile("cp.async.bulk.prefetch.tensor.5d.L2.global.tile [%0, {%1, %2, %3, %4, %5}];\n" ::
+                   "l"(reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_load_5d(void* smem_dst, const CUtensorMap* map,
                                             uint64_t* bar, int c0, int c1, int c2, int c3,
                                             int c4) {

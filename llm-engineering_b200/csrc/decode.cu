@@ -39,6 +39,10 @@ namespace {
 using namespace b2p;
 
 constexpr int kSub = 16;  // slots per sub-block = tokens per MMA tile
+// Sub-blocks per warp prefetched into L2 before the dependent-launch wait (at most 32).
+// Measured on the 256-sequence workload: 104.8 us per launch with 4, 105.2 with 8, 106.6
+// with 16, 105.6 without.
+constexpr int kL2Prefetch = 4;
 
 struct DecodeParams {
   const uint8_t* q;
@@ -359,6 +363,17 @@ __global__ void __launch_bounds__(W * 32) paged_decode_tc(const __grid_constant_
     }
     issued = k + 1;
   };
+  // While the previous kernel finishes (this CTA may start early under programmatic
+  // dependent launch, when HBM is mostly idle), pull the warp's first sub-blocks into L2:
+  // lane j prefetches item j's K and V boxes. The prefetches write no shared memory, so
+  // they need no wait of their own; the loads after the wait then hit L2.
+  if (lane < kL2Prefetch && lane < n && slot_lo >= 0 && slot_lo < num_slots) {
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      tma_prefetch_l2_5d(&kmap, 0, c, head, (int)slot_lo, p.layer);
+      tma_prefetch_l2_5d(&vmap, 0, c, head, (int)slot_lo, p.layer);
+    }
+  }
   pdl_wait();  // the first access to memory the previous kernel may write
   for (int64_t k = 0; k < S && k < n; ++k) issue(k);
   if (empties_warp) write_empties();  // while the first tiles are in flight
